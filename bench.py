@@ -1,0 +1,527 @@
+#!/usr/bin/env python
+"""Benchmark of the batched FP32 Cholesky hot path (custom_kernel) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU, NCCL)
+
+A *step* is one ``custom_kernel`` call over one (batch, n, n) input. Inputs are
+BASELINE.json's seeded synthetic families (linalg_kernels_b200.inputs), resident in HBM
+before timing, taken round-robin from a pool of distinct inputs whose total size exceeds
+twice the 126 MB L2 (no L2 reuse between steps). Timing: W warm-up steps, barrier +
+synchronize, CUDA events around exactly K steps on the launching queue, barrier +
+synchronize, maximum over ranks. Multi-GPU: every rank factors its own batch of the
+configured size (independent matrices, no collective on the data path): weak scaling.
+
+Printed (rank 0, one JSON line): value = matrices/s over all ranks; TFLOP/s at n^3/3 per
+matrix; roofline of the dominant kernel (achieved / MEASURED_PEAKS.json peak; traffic from
+the committed ncu capture); e2e = the same metric through the C ABI with pinned host
+buffers and both copies inside the timed region; cpu_baseline = the reference's own CPU
+path (torch.linalg.cholesky_ex on the host cores) on a bounded sample; clocks sampled by
+nvidia-smi during the run; gpu_launches = our kernel launches in the timed region.
+``--impl reference`` times that CPU path alone as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+DEFAULT_CONFIG = "b1024n64"
+L2_BYTES = 126 * 1024 * 1024
+
+# The reference's published single-B200 times for these shapes,
+# converted to matrices/s: batch / time.
+REFERENCE_PUBLISHED_S = {
+    "b4096n32": 15.7e-6, "b1024n64": 24.1e-6, "b64n256": 191e-6, "b640n512": 2.88e-3,
+    "b60n1024": 2.20e-3, "b1n16384": 15.1e-3, "b1n32768": 42.9e-3,
+}
+
+# DRAM bytes (read + write) per launch of the dominant kernel from one ncu capture of the
+# same workload: profiles/<kernel>_<workload>.md (null until captured).
+NCU_TRAFFIC_BYTES: dict[str, float | None] = {}
+
+
+def _peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# --------------------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------------------
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier(device_ids=[self.local])
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# --------------------------------------------------------------------------------------
+# clocks during the run
+# --------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict | None:
+        rows = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append({"sm": float(parts[1]), "max": float(parts[2]),
+                             "power": float(parts[3]) if parts[3] not in ("[N/A]", "") else 0.0,
+                             "hw_slowdown": parts[5], "hw_thermal": parts[6],
+                             "sw_thermal": parts[7], "sw_power_cap": parts[8]})
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        peak_power = max(r["power"] for r in rows)
+        loaded = [r for r in rows if r["power"] >= 0.5 * peak_power] or rows
+        reasons = set()
+        for r in rows:
+            for key, name in (("hw_slowdown", "hw_slowdown"), ("hw_thermal", "hw_thermal_slowdown"),
+                              ("sw_thermal", "sw_thermal_slowdown"),
+                              ("sw_power_cap", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
+                "sm_max_mhz": max(r["max"] for r in rows), "reasons": sorted(reasons),
+                "samples": len(rows), "samples_under_load": len(loaded),
+                "power_w_max": peak_power,
+                "window": "nvidia-smi every 100 ms over warm-up + timed steps"}
+
+
+# --------------------------------------------------------------------------------------
+# helpers
+# --------------------------------------------------------------------------------------
+def _pool(cfg, device, rank: int, max_inputs: int):
+    from linalg_kernels_b200 import inputs
+
+    in_bytes = cfg.batch * cfg.n * cfg.n * 4
+    count = 1 if in_bytes >= 2 * L2_BYTES else min(max_inputs, math.ceil(2 * L2_BYTES / in_bytes))
+    pool = []
+    cond = None
+    for i in range(count):
+        c = inputs.Config(cfg.name, cfg.batch, cfg.n, cfg.family, cfg.param,
+                          cfg.seed + 7919 * i + 104729 * rank)
+        a, cnd = inputs.config_input(c, device=device)
+        pool.append(a)
+        if cond is None:
+            cond = cnd
+    return pool, in_bytes * count
+
+
+def _time_steps(fn, pool, steps: int, warmup: int, dist: Dist):
+    """W untimed steps, then exactly K timed steps; returns (total_ms, per_step_ms list)."""
+    for i in range(warmup):
+        fn(pool[i % len(pool)])
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    q = torch.cuda.current_stream()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    start.record(q)
+    for i in range(steps):
+        ev[i][0].record(q)
+        fn(pool[i % len(pool)])
+        ev[i][1].record(q)
+    end.record(q)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    total = start.elapsed_time(end)
+    per = [a.elapsed_time(b) for a, b in ev]
+    return total, per
+
+
+def _cpu_reference_rate(cfg, a_host: torch.Tensor, budget_s: float) -> dict:
+    """The reference's CPU path (submission.py:7 on CPU tensors: LAPACK via MKL) on a
+    bounded sample of the workload; all host threads."""
+    from oracle import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
+    per_mat = cfg.n ** 3 / 3.0
+    # sample: whole batch if it is cheap, else a prefix of the batch (at least 1 matrix)
+    sample_b = a_host.shape[0]
+    x = a_host[:1]
+    t0 = time.perf_counter()
+    oracle.reference_factor(x)
+    one = max(time.perf_counter() - t0, 1e-6)
+    if one * sample_b > budget_s:
+        sample_b = max(1, int(budget_s / one))
+    x = a_host[:sample_b].contiguous()
+    oracle.reference_factor(x)  # warm
+    reps, times = 0, []
+    t_end = time.perf_counter() + budget_s
+    while reps < 3 or (time.perf_counter() < t_end and reps < 50):
+        t0 = time.perf_counter()
+        oracle.reference_factor(x)
+        times.append(time.perf_counter() - t0)
+        reps += 1
+        if cfg.n >= 8192:
+            break
+    med = statistics.median(times)
+    return {"value": sample_b / med, "unit": "matrices/s", "cores": threads, "kind": "reference",
+            "sample": f"{sample_b} of {cfg.batch} matrices of n={cfg.n}, median of {reps} runs "
+                      f"of torch.linalg.cholesky_ex on CPU (MKL LAPACK spotrf)",
+            "tflops": sample_b * per_mat / med / 1e12,
+            "cpu": _cpu_model()}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# --------------------------------------------------------------------------------------
+# arms
+# --------------------------------------------------------------------------------------
+def run_reference(args, dist: Dist):
+    """Reference arm: the reference's own CPU implementation of the path on the host cores."""
+    from linalg_kernels_b200 import inputs
+
+    cfg = inputs.CONFIGS[args.config]
+    if dist.rank != 0:
+        return
+    if torch.cuda.is_available():
+        a, _ = inputs.config_input(cfg, device="cuda")
+        a_host = a.cpu()
+        del a
+    else:
+        a_host, _ = inputs.config_input(cfg, device="cpu", batch=min(cfg.batch, 64))
+    # each step: a bounded sample of the workload (about 1 s of CPU work at most)
+    base = _cpu_reference_rate(cfg, a_host, budget_s=1.0)
+    sample_b = int(base["sample"].split(" ")[0])
+    x = a_host[:sample_b].contiguous()
+    from oracle import oracle
+
+    for _ in range(args.warmup):
+        oracle.reference_factor(x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.reference_factor(x)
+    dt = time.perf_counter() - t0
+    value = sample_b * args.steps / dt
+    line = {
+        "impl": "reference", "metric": "matrices/s", "value": value, "unit": "matrices/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "tflops": value * cfg.n ** 3 / 3.0 / 1e12,
+        "config": {"workload": cfg.name, "batch": cfg.batch, "n": cfg.n,
+                   "family": cfg.family, "seed": cfg.seed,
+                   "step": f"torch.linalg.cholesky_ex on {sample_b} host matrices"},
+        "cpu_baseline": {"value": value, "unit": "matrices/s", "cores": base["cores"],
+                         "kind": "reference", "sample": base["sample"], "cpu": base["cpu"]},
+        "e2e": {"value": value, "unit": "matrices/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, dist: Dist):
+    from linalg_kernels_b200 import _lib, inputs
+    from linalg_kernels_b200.cholesky import custom_kernel
+
+    lib = _lib.load()
+    dev = torch.device("cuda", dist.local if dist.world > 1 else 0)
+    torch.cuda.set_device(dev)
+    peaks, peak_kind = _peaks()
+    cfg = inputs.CONFIGS[args.config]
+    n, b = cfg.n, cfg.batch
+    pool, pool_bytes = _pool(cfg, dev, dist.rank, max_inputs=32)
+    launches_per_call = int(lib.chol_launch_count(b, n))
+
+    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dev.index)).split(",")[dev.index]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else dev.index
+    with ClockSampler(gpu_index) as clocks:
+        total_ms, per = _time_steps(custom_kernel, pool, args.steps, args.warmup, dist)
+    total_ms = dist.max(total_ms)
+    ms_step = total_ms / args.steps
+    value = dist.world * b * args.steps / (total_ms / 1e3)
+    tflops = value * n ** 3 / 3.0 / 1e12
+
+    # dominant kernel roofline
+    roof = _roofline(args, cfg, per, peaks, peak_kind, lib, pool, dev, dist)
+
+    # end to end through the C ABI: pinned host in -> device -> factor -> pinned host out
+    e2e = _e2e(args, cfg, pool, lib, dev, dist)
+
+    cpu = None
+    if dist.world == 1 and not args.no_cpu_baseline:
+        cpu = _cpu_reference_rate(cfg, pool[0].cpu(), budget_s=args.cpu_budget)
+
+    shapes = None
+    if dist.world == 1 and args.shapes:
+        shapes = _other_shapes(args, cfg.name, dev, peaks, peak_kind, lib)
+
+    line = {
+        "metric": "matrices/s", "value": value, "unit": "matrices/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": (value / (b / REFERENCE_PUBLISHED_S[cfg.name])
+                        if dist.world == 1 and cfg.name in REFERENCE_PUBLISHED_S else None),
+        "dtype": "f32", "data": "synthetic",
+        "tflops": tflops,
+        "config": {"workload": cfg.name, "batch": b, "n": n, "global_batch": b * dist.world,
+                   "family": cfg.family, "param": cfg.param, "seed": cfg.seed,
+                   "parallelism": f"batch-sharded x{dist.world} (independent matrices, "
+                                  f"no collective)",
+                   "l2": f"round-robin over {len(pool)} distinct resident inputs "
+                         f"({pool_bytes / 2**20:.0f} MiB > 2x L2)"},
+        "roofline": roof,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
+        "gpu_launches": launches_per_call * args.steps,
+        "launches_per_step": launches_per_call,
+    }
+    if shapes is not None:
+        line["shapes"] = shapes
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def _roofline(args, cfg, per_step_ms, peaks, peak_kind, lib, pool, dev, dist):
+    n, b = cfg.n, cfg.batch
+    if n <= 256 and int(lib.chol_launch_count(b, n)) == 1:
+        # single launch per step: the step's event pair is the kernel's duration
+        t = dist.max(statistics.mean(per_step_ms)) / 1e3
+        bytes_ = 8.0 * n * n * b
+        achieved = bytes_ / t / 1e9
+        peak = peaks["hbm_gbs"]
+        return {"bound": "hbm", "kernel": "small_potrf_kernel", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_kind": f"{peak_kind} hbm_gbs (burst copy)",
+                "traffic": NCU_TRAFFIC_BYTES.get(cfg.name),
+                "algorithmic_bytes_per_launch": bytes_, "launch_ms": t * 1e3}
+    # blocked path: time the largest trailing update launch alone (its own CUDA events)
+    return _gemm_roofline(cfg, peaks, peak_kind, lib, pool, dev, dist)
+
+
+def _gemm_roofline(cfg, peaks, peak_kind, lib, pool, dev, dist):
+    from linalg_kernels_b200 import _lib
+
+    n, b = cfg.n, cfg.batch
+    kdim = 64 if n <= 1024 else 512
+    m = n - kdim
+    a = pool[0]
+    c = torch.empty_like(a)
+    q = ctypes.c_void_p(_lib.current_queue(dev))
+
+    def launch():
+        st = lib.chol_gemm_nt_f32(
+            ctypes.c_void_p(c.data_ptr() + (kdim * n + kdim) * 4), b, n * n, n, m, m, kdim,
+            ctypes.c_void_p(a.data_ptr() + kdim * n * 4), n * n, n,
+            ctypes.c_void_p(a.data_ptr() + kdim * n * 4), n * n, n,
+            -1.0, 1.0, 0, 1, q)
+        _lib.check(st, "chol_gemm_nt_f32")
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    reps = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    t = dist.max(e0.elapsed_time(e1) / reps) / 1e3
+    flops = 2.0 * b * (m * (m + 1) / 2) * kdim  # lower triangle incl. diagonal
+    achieved = flops / t / 1e12
+    peak = peaks["bf16_tflops"] / 2.0  # TF32 dense rate is half the bf16 rate on tcgen05
+    return {"bound": "tensor", "kernel": "trailing update C -= P P^T (lower tiles)",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_kind": f"{peak_kind} bf16_tflops / 2 (TF32 rate)",
+            "traffic": NCU_TRAFFIC_BYTES.get(cfg.name + "/update"),
+            "shape": {"m": m, "k": kdim, "batch": b}, "launch_ms": t * 1e3}
+
+
+def _e2e(args, cfg, pool, lib, dev, dist):
+    from linalg_kernels_b200 import _lib
+
+    n, b = cfg.n, cfg.batch
+    nbytes = b * n * n * 4
+    hosts = [p.cpu().pin_memory() for p in pool[: min(len(pool), 2)]]
+    out_h = torch.empty(b, n, n).pin_memory()
+    a_d = torch.empty(b, n, n, device=dev)
+    l_d = torch.empty(b, n, n, device=dev)
+    q_int = _lib.current_queue(dev)
+
+    def step(i):
+        a_d.copy_(hosts[i % len(hosts)], non_blocking=True)
+        st = lib.chol_potrf_batched_f32(ctypes.c_void_p(a_d.data_ptr()),
+                                        ctypes.c_void_p(l_d.data_ptr()), b, n, None,
+                                        ctypes.c_void_p(q_int))
+        _lib.check(st, "chol_potrf_batched_f32")
+        out_h.copy_(l_d, non_blocking=True)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(e0.elapsed_time(e1))
+    return {"value": dist.world * b * args.steps / (ms / 1e3), "unit": "matrices/s",
+            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+            "ms_per_step": ms / args.steps,
+            "path": "chol_potrf_batched_f32 (C ABI) with pinned host input/output"}
+
+
+def _other_shapes(args, skip, dev, peaks, peak_kind, lib):
+    from linalg_kernels_b200 import inputs
+    from linalg_kernels_b200.cholesky import custom_kernel
+
+    out = []
+    names = [k for k in inputs.CONFIGS if k != skip and (args.big or k != "b1n32768")]
+    for name in names:
+        cfg = inputs.CONFIGS[name]
+        pool, pool_bytes = _pool(cfg, dev, 0, max_inputs=16)
+        steps = max(3, min(args.steps, 20))
+        total, per = _time_steps(custom_kernel, pool, steps, 3, _NoDist())
+        ms = total / steps
+        value = cfg.batch / (ms / 1e3)
+        row = {"workload": name, "ms_per_step": ms, "matrices_per_s": value,
+               "tflops": value * cfg.n ** 3 / 3.0 / 1e12,
+               "reference_ms": REFERENCE_PUBLISHED_S[name] * 1e3,
+               "vs_reference_published": REFERENCE_PUBLISHED_S[name] * 1e3 / ms}
+        if cfg.n <= 256:
+            row["hbm_frac_of_measured"] = 8.0 * cfg.n ** 2 * cfg.batch / (ms / 1e3) / 1e9 / \
+                peaks["hbm_gbs"]
+        else:
+            row["tf32_frac_of_measured"] = row["tflops"] / (peaks["bf16_tflops"] / 2.0)
+        out.append(row)
+        del pool
+        torch.cuda.empty_cache()
+    return out
+
+
+class _NoDist(Dist):
+    def __init__(self):
+        self.world, self.rank, self.local, self.pg = 1, 0, 0, None
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default=DEFAULT_CONFIG)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0,
+                    help="seconds of CPU work for the cpu_baseline sample")
+    ap.add_argument("--shapes", action=argparse.BooleanOptionalAction, default=True,
+                    help="also time the other BASELINE shapes (N=1 only)")
+    ap.add_argument("--big", action="store_true", help="include b1n32768 in --shapes")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        # the CPU reference arm runs on rank 0 only; other ranks exit without work
+        nd = _NoDist()
+        nd.rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, nd)
+        return
+    dist = Dist()
+    try:
+        run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,146 @@
+/*
+ * chol_b200.h — C ABI of the B200 (sm_100a) batched FP32 Cholesky library.
+ *
+ * This is the drop-in boundary for the reference's single hot path,
+ *   custom_kernel(data: (b, n, n) float32 SPD) -> L (lower, exact-zero upper)
+ * of Mark123M/linalg-kernels:
+ *   - submission.py:6-7           (torch.linalg.cholesky_ex(data, check_errors=False).L)
+ *   - cholesky/cholesky.py:5845-5850  (custom_kernel: exact-shape dispatch, torch fallback)
+ *   - cholesky/cholesky.py:232-250, 391-409, 2598-2656, 3373-3435, 5764-5802
+ *     (the per-shape pybind entry points `run(data) -> L` that the dispatcher calls)
+ *
+ * The reference binds per-shape C++ through pybind (`m.def("run", ...)`) and throws
+ * `TORCH_CHECK` errors. Here one set of plain-C entry points covers every (b, n):
+ * pointers, sizes and an opaque queue handle in, an integer status out. No torch types,
+ * no C++ exceptions cross this boundary.
+ *
+ * Layout: A and L are row-major contiguous (batch, n, n) float32 arrays in device
+ * memory (matrix m starts at m*n*n). Only the lower triangle of A is read (LAPACK
+ * uplo='L', which is what torch.linalg.cholesky uses). A is never written unless
+ * A == L (exact in-place). L receives the factor with exact zeros above the diagonal.
+ *
+ * `queue` is a cudaStream_t passed as void* (NULL = the legacy default queue). All work
+ * is enqueued asynchronously on it; the call returns before the GPU finishes.
+ *
+ * Status codes (int): see CHOL_* below. Non-SPD input is reported per matrix in `info`
+ * (LAPACK convention: 0 = success, k > 0 = the leading minor of order k is not positive
+ * definite); the factor of such a matrix is unspecified from column k on, as with
+ * torch.linalg.cholesky_ex(check_errors=False).
+ */
+#ifndef CHOL_B200_H
+#define CHOL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CHOL_API __attribute__((visibility("default")))
+#else
+#define CHOL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CHOL_OK 0
+#define CHOL_ERR_INVALID_ARG 1   /* bad shape, null pointer, partial aliasing */
+#define CHOL_ERR_LAUNCH 2        /* a kernel launch failed (cudaGetLastError) */
+#define CHOL_ERR_NOT_SPD 3       /* reported by chol_info_check when some info[m] > 0 */
+#define CHOL_ERR_WAIT_TIMEOUT 4  /* a bounded device-side wait ran out (status word set) */
+#define CHOL_ERR_WORKSPACE 5     /* caller workspace missing or smaller than required */
+#define CHOL_ERR_DEVICE 6        /* no usable sm_100 device / CUDA runtime error */
+#define CHOL_ERR_UNSUPPORTED 7   /* size outside what this build supports */
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+CHOL_API int chol_version(void);
+
+/* Human-readable text for a status code (static storage, never NULL). */
+CHOL_API const char* chol_strerror(int status);
+
+/*
+ * One-time per-device set-up: checks the device is sm_100, raises the dynamic
+ * shared-memory limits of the kernels and resolves driver entry points (TMA maps).
+ * Replaces the reference's per-module `prepare()` (cholesky/cholesky.py:2590-2596,
+ * called from the lazily-built module, :5807-5820). Idempotent and thread-safe; the
+ * factor entry points call it implicitly, but calling it before any CUDA-graph capture
+ * keeps the attribute calls out of the capture.
+ */
+CHOL_API int chol_prepare(int device);
+
+/*
+ * Bytes of device workspace chol_potrf_batched_ws_f32 needs for (batch, n).
+ * 0 when the chosen kernels need none (small n).
+ */
+CHOL_API size_t chol_workspace_bytes(int64_t batch, int64_t n);
+
+/*
+ * Batched Cholesky, library-managed workspace.
+ * Replaces custom_kernel(data) -> L (cholesky/cholesky.py:5845-5850; submission.py:6-7):
+ * the caller allocates L (the reference allocates it with at::empty_like inside the
+ * per-shape C++ entry point, e.g. cholesky/cholesky.py:2603, :5766).
+ *   A, L   : device pointers to batch*n*n floats; A == L allowed (in place), partial overlap rejected
+ *   info   : NULL or device pointer to batch ints (written on the queue)
+ *   queue  : cudaStream_t as void*
+ * The workspace (if the size needs one) is a per-device cache grown with cudaMalloc on
+ * first use for a size; call chol_potrf_batched_ws_f32 to supply your own instead.
+ */
+CHOL_API int chol_potrf_batched_f32(const float* A, float* L, int64_t batch, int64_t n,
+                           int* info, void* queue);
+
+/*
+ * Same as chol_potrf_batched_f32 with caller-provided device workspace of at least
+ * chol_workspace_bytes(batch, n) bytes (256-byte aligned). Makes no allocation; this is
+ * the form the Python wrapper uses (the workspace comes from torch's caching allocator).
+ */
+CHOL_API int chol_potrf_batched_ws_f32(const float* A, float* L, int64_t batch, int64_t n,
+                              int* info, void* workspace, size_t workspace_bytes,
+                              void* queue);
+
+/*
+ * Number of kernel launches one chol_potrf_batched_*_f32 call makes for (batch, n)
+ * (host-only arithmetic on the launch plan; no device call). Used to report launch counts.
+ */
+CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
+
+/*
+ * Host-side helper: copies info (batch ints, device) to the host after synchronising
+ * the queue and returns CHOL_ERR_NOT_SPD if any entry is > 0 (first failing matrix in
+ * *first_bad, or -1). torch.linalg.cholesky (check_errors=True) behaviour; the
+ * reference's custom_kernel never checks (check_errors=False, cholesky/cholesky.py:5850).
+ */
+CHOL_API int chol_info_check(const int* info, int64_t batch, void* queue, int64_t* first_bad);
+
+/*
+ * Building blocks of the blocked path, exported for the multi-GPU block-column-cyclic
+ * driver (which owns the panel schedule and the NCCL broadcasts) and for tests. Each acts
+ * on `batch` row-major matrices spaced `stride` floats apart with leading dimension `ld`
+ * (floats). They correspond to the steps of the reference's single-GPU schedule:
+ * factor128_kernel (diagonal block + its inverse), gemm_apply (X * T^T) and
+ * gemm_history / gemm_inner (C -= P * Q^T) at cholesky/cholesky.py:5440-5489, 5670-5690,
+ * 5625-5668. The reference has no multi-GPU path.
+ */
+
+/* Factor the kb x kb diagonal block at (k, k) in place (1 <= kb <= 64), zero its strict
+   upper part, and, if Tinv is not NULL, write inv(L[k:k+kb, k:k+kb]) as a row-major
+   64 x 64 lower triangle at Tinv + m*4096 (identity beyond kb). info (nullable): first
+   non-positive pivot column (1-based, global), written when k == 0 or info[m] == 0. */
+CHOL_API int chol_block_potrf_f32(float* L, int64_t batch, int64_t stride, int64_t ld, int64_t k,
+                         int64_t kb, float* Tinv, int* info, void* queue);
+
+/* C[r][c] = alpha * sum_{q<K} P[r][q] * Q[c][q] + beta * C[r][c] for r < m, c < ncols,
+   where C, P, Q point at the (0, 0) element of their views (row-major, K contiguous in
+   P and Q). lower_only != 0 writes only elements with c <= r + diag_offset. With beta
+   == 0 and ncols <= 64, C may alias P (the panel solve X <- X * T^T runs in place).
+   Runs on the tensor cores (tcgen05, 3xTF32 split) where the shape allows, else on
+   FP32 FMA. */
+CHOL_API int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t ldc, int64_t m,
+                     int64_t ncols, int64_t K, const float* P, int64_t pstride, int64_t ldp,
+                     const float* Q, int64_t qstride, int64_t ldq, float alpha, float beta,
+                     int64_t diag_offset, int lower_only, void* queue);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CHOL_B200_H */

@@ -1,0 +1,97 @@
+"""ctypes binding of ``libchol_b200.so`` (the C ABI declared in include/chol_b200.h).
+
+The library is loaded from the package directory. If it is missing, importing the
+compute entry points raises: there is no CPU or torch fallback on the product path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libchol_b200.so"
+
+# status codes, as in include/chol_b200.h
+CHOL_OK = 0
+CHOL_ERR_INVALID_ARG = 1
+CHOL_ERR_LAUNCH = 2
+CHOL_ERR_NOT_SPD = 3
+CHOL_ERR_WAIT_TIMEOUT = 4
+CHOL_ERR_WORKSPACE = 5
+CHOL_ERR_DEVICE = 6
+CHOL_ERR_UNSUPPORTED = 7
+
+_i64 = ctypes.c_int64
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_int = ctypes.c_int
+_f32 = ctypes.c_float
+
+# name -> (restype, argtypes); every function include/chol_b200.h declares
+SIGNATURES: dict[str, tuple] = {
+    "chol_version": (_int, []),
+    "chol_strerror": (ctypes.c_char_p, [_int]),
+    "chol_prepare": (_int, [_int]),
+    "chol_workspace_bytes": (_sz, [_i64, _i64]),
+    "chol_potrf_batched_f32": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
+    "chol_potrf_batched_ws_f32": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
+    "chol_launch_count": (_i64, [_i64, _i64]),
+    "chol_info_check": (_int, [_vp, _i64, _vp, ctypes.POINTER(_i64)]),
+    "chol_block_potrf_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "chol_gemm_nt_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64,
+                                _vp, _i64, _i64, _f32, _f32, _i64, _int, _vp]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class CholeskyError(RuntimeError):
+    """A non-zero status from the C ABI."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        super().__init__(f"{where}: {strerror(status)} (status {status})")
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load (once) and return the library with every signature bound."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise ImportError(
+                f"{p} is missing: build it with `python -m linalg_kernels_b200.build` "
+                "(this package has no CPU fallback)")
+        lib = ctypes.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def strerror(status: int) -> str:
+    try:
+        return load().chol_strerror(int(status)).decode()
+    except ImportError:
+        return f"status {status}"
+
+
+def check(status: int, where: str) -> None:
+    if status != CHOL_OK:
+        raise CholeskyError(status, where)
+
+
+def current_queue(device) -> int:
+    """Raw handle of torch's current CUDA queue on ``device`` (0 = legacy default)."""
+    import torch
+
+    return int(torch.cuda.current_stream(device).cuda_stream)

@@ -1,0 +1,97 @@
+"""Drop-in batched FP32 Cholesky for B200: ``custom_kernel(data) -> L``.
+
+Mirrors the reference entry point ``custom_kernel`` (cholesky/cholesky.py:5845-5850,
+submission.py:6-7): input a ``(b, n, n)`` float32 CUDA tensor, symmetric positive
+definite up to FP32 roundoff; output a new float32 tensor of the same shape holding the
+lower-triangular factor L (positive diagonal, exact zeros above the diagonal) with
+``A = L @ L.T``. The input is never written.
+
+Where the reference dispatches exact benchmark shapes to per-shape modules and sends every
+other input to ``torch.linalg.cholesky_ex`` (cholesky/cholesky.py:5846-5850), this module
+sends every CUDA float32 input to the hand-written sm_100a kernels through the C ABI of
+``libchol_b200.so``. Inputs the reference would have handed to torch on the CPU (CPU
+tensors, other dtypes) raise ``TypeError`` instead: the B200 build has no CPU path.
+Non-contiguous CUDA inputs are made contiguous first (a device copy).
+
+Non-SPD input is not an error here, as in the reference (``check_errors=False``); use
+``cholesky_ex`` for the per-matrix ``info`` or ``cholesky`` to raise on failure.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+__all__ = ["custom_kernel", "cholesky_ex", "cholesky", "workspace_bytes"]
+
+
+def _prepare_input(data: torch.Tensor) -> tuple[torch.Tensor, int, int]:
+    if not isinstance(data, torch.Tensor):
+        raise TypeError("custom_kernel expects a torch.Tensor")
+    if not data.is_cuda:
+        raise TypeError("custom_kernel runs on the GPU only: move the input to a CUDA device "
+                        "(this build has no CPU fallback)")
+    if data.dtype != torch.float32:
+        raise TypeError(f"custom_kernel expects float32 input, got {data.dtype}")
+    if data.dim() < 2 or data.shape[-1] != data.shape[-2]:
+        raise ValueError(f"expected (..., n, n) input, got shape {tuple(data.shape)}")
+    if not data.is_contiguous():
+        data = data.contiguous()
+    n = int(data.shape[-1])
+    batch = 1
+    for s in data.shape[:-2]:
+        batch *= int(s)
+    return data, batch, n
+
+
+def workspace_bytes(batch: int, n: int) -> int:
+    """Device scratch the factorisation of ``batch`` n x n matrices needs."""
+    return int(_lib.load().chol_workspace_bytes(int(batch), int(n)))
+
+
+def _factor(data: torch.Tensor, want_info: bool):
+    data, batch, n = _prepare_input(data)
+    lib = _lib.load()
+    out = torch.empty_like(data)
+    info = torch.zeros(data.shape[:-2], dtype=torch.int32, device=data.device) if want_info \
+        else None
+    if batch == 0 or n == 0:
+        return out, info
+    with torch.cuda.device(data.device):
+        need = int(lib.chol_workspace_bytes(batch, n))
+        ws = torch.empty(need, dtype=torch.uint8, device=data.device) if need else None
+        queue = _lib.current_queue(data.device)
+        status = lib.chol_potrf_batched_ws_f32(
+            ctypes.c_void_p(data.data_ptr()), ctypes.c_void_p(out.data_ptr()), batch, n,
+            ctypes.c_void_p(info.data_ptr()) if info is not None else None,
+            ctypes.c_void_p(ws.data_ptr()) if ws is not None else None, need,
+            ctypes.c_void_p(queue))
+    _lib.check(status, "chol_potrf_batched_ws_f32")
+    return out, info
+
+
+def custom_kernel(data: torch.Tensor) -> torch.Tensor:
+    """Lower Cholesky factor of a batch of SPD matrices (reference: cholesky.py:5845)."""
+    return _factor(data, want_info=False)[0]
+
+
+def cholesky_ex(data: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(L, info)`` like ``torch.linalg.cholesky_ex``: info[m] = 0 on success, else the
+    order of the leading minor that is not positive definite (LAPACK convention)."""
+    return _factor(data, want_info=True)
+
+
+def cholesky(data: torch.Tensor) -> torch.Tensor:
+    """Like ``torch.linalg.cholesky``: raises ``torch.linalg.LinAlgError`` on non-SPD input."""
+    out, info = cholesky_ex(data)
+    bad = torch.nonzero(info.reshape(-1) > 0)
+    if bad.numel():
+        m = int(bad[0, 0])
+        raise torch.linalg.LinAlgError(
+            f"cholesky: the factorization could not be completed because the input is not "
+            f"positive-definite (batch element {m}, leading minor of order "
+            f"{int(info.reshape(-1)[m])})")
+    return out

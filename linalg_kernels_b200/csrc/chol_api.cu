@@ -1,0 +1,347 @@
+// chol_api.cu — the C-ABI entry points and the host-side launch schedule.
+//
+// Mirrors the reference boundary custom_kernel(data) -> L (cholesky/cholesky.py:5845-5850):
+// where the reference routes exact shapes to per-shape modules and sends everything else
+// to torch, this library plans every (batch, n) on the GPU:
+//   n <= 64   one launch of the warp-register kernel (chol_small.cu)
+//   n  > 64   right-looking blocked schedule, 64-wide diagonal blocks, outer panels of
+//             width NB whose trailing update is deferred to one rank-NB update:
+//               copy tril(A) -> L
+//               for each outer panel [K0, K0+NB):
+//                 for each 64-wide block k in the panel:
+//                   potrf_block(k)            factor + inverse T_k   (1 CTA / matrix)
+//                   X = L[k+64:, k] * T_k^T   panel solve, in place  (GEMM)
+//                   L[k+64:, k+64:K0+NB] -= X * X[..]^T  in-panel update (GEMM, K = 64)
+//                 L[K0+NB:, K0+NB:] -= P * P^T, P = L[K0+NB:, K0:K0+NB]  (lower tiles, K = NB)
+// All launches go on the caller's queue with programmatic dependent launch.
+#include <mutex>
+#include <vector>
+
+#include "chol_common.cuh"
+
+namespace chol {
+
+namespace {
+
+constexpr int64_t kBlock = 64;
+
+int64_t outer_width(int64_t n) {
+  // n <= 1024: one outer panel (plain right-looking with 64-wide steps); larger: 512.
+  return n <= 1024 ? n : 512;
+}
+
+struct DeviceState {
+  std::once_flag once;
+  int status = CHOL_OK;
+  std::mutex ws_mu;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+
+DeviceState* device_state(int dev) {
+  static DeviceState states[64];
+  if (dev < 0 || dev >= 64) return nullptr;
+  return &states[dev];
+}
+
+int prepare_device(int dev) {
+  DeviceState* st = device_state(dev);
+  if (!st) return CHOL_ERR_DEVICE;
+  std::call_once(st->once, [&]() {
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      st->status = CHOL_ERR_DEVICE;
+      return;
+    }
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) {
+      st->status = CHOL_ERR_DEVICE;
+      return;
+    }
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10) {
+      st->status = CHOL_ERR_DEVICE;
+    } else if (prepare_small() != cudaSuccess || prepare_kernels(dev) != CHOL_OK) {
+      st->status = CHOL_ERR_DEVICE;
+    }
+    if (prev != dev) cudaSetDevice(prev);
+  });
+  return st->status;
+}
+
+bool overlaps_partially(const float* a, const float* b, int64_t count) {
+  if (a == b) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  const uintptr_t bytes = uintptr_t(count) * sizeof(float);
+  return a0 < b0 + bytes && b0 < a0 + bytes;
+}
+
+size_t blocked_workspace(int64_t batch, int64_t n) {
+  if (n <= 64) return 0;
+  return size_t(batch) * kBlock * kBlock * sizeof(float);
+}
+
+int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, float* Tws,
+                cudaStream_t q) {
+  int st = launch_copy_lower(A, L, batch, n, q, true);
+  if (st) return st;
+  const int64_t mstride = n * n;
+  const int64_t NB = outer_width(n);
+  for (int64_t K0 = 0; K0 < n; K0 += NB) {
+    const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
+    for (int64_t k = K0; k < K0 + KB; k += kBlock) {
+      const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
+      st = launch_potrf_block(L, mstride, n, L, mstride, n, batch, k, kb, Tws, info, q, true);
+      if (st) return st;
+      const int64_t below = n - k - kb;
+      if (below <= 0) continue;
+      // panel solve: L[k+kb:, k:k+kb] <- L[k+kb:, k:k+kb] * T^T (in place)
+      GemmArgs s{};
+      s.C = L + (k + kb) * n + k;
+      s.cstride = mstride;
+      s.ldc = n;
+      s.P = s.C;
+      s.pstride = mstride;
+      s.ldp = n;
+      s.Q = Tws;
+      s.qstride = kBlock * kBlock;
+      s.ldq = kBlock;
+      s.m = below;
+      s.ncols = kb;
+      s.K = kb;
+      s.alpha = 1.f;
+      s.beta = 0.f;
+      s.lower_only = 0;
+      s.batch = batch;
+      st = launch_gemm_simt(s, q, true);
+      if (st) return st;
+      const int64_t inpanel = K0 + KB - k - kb;
+      if (inpanel > 0) {
+        GemmArgs u{};
+        u.C = L + (k + kb) * n + (k + kb);
+        u.cstride = mstride;
+        u.ldc = n;
+        u.P = L + (k + kb) * n + k;
+        u.pstride = mstride;
+        u.ldp = n;
+        u.Q = u.P;
+        u.qstride = mstride;
+        u.ldq = n;
+        u.m = below;
+        u.ncols = inpanel;
+        u.K = kb;
+        u.alpha = -1.f;
+        u.beta = 1.f;
+        u.diag_offset = 0;
+        u.lower_only = 1;
+        u.batch = batch;
+        st = launch_gemm_simt(u, q, true);
+        if (st) return st;
+      }
+    }
+    const int64_t rest = n - K0 - KB;
+    if (rest > 0) {
+      GemmArgs t{};
+      t.C = L + (K0 + KB) * n + (K0 + KB);
+      t.cstride = mstride;
+      t.ldc = n;
+      t.P = L + (K0 + KB) * n + K0;
+      t.pstride = mstride;
+      t.ldp = n;
+      t.Q = t.P;
+      t.qstride = mstride;
+      t.ldq = n;
+      t.m = rest;
+      t.ncols = rest;
+      t.K = KB;
+      t.alpha = -1.f;
+      t.beta = 1.f;
+      t.diag_offset = 0;
+      t.lower_only = 1;
+      t.batch = batch;
+      st = launch_gemm_simt(t, q, true);
+      if (st) return st;
+    }
+  }
+  return CHOL_OK;
+}
+
+// Launch count of run_blocked for (batch, n); keep in step with the schedule above.
+int64_t blocked_launches(int64_t n) {
+  int64_t count = 1;  // copy_lower
+  const int64_t NB = outer_width(n);
+  for (int64_t K0 = 0; K0 < n; K0 += NB) {
+    const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
+    for (int64_t k = K0; k < K0 + KB; k += kBlock) {
+      const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
+      count += 1;
+      if (n - k - kb <= 0) continue;
+      count += 1;
+      if (K0 + KB - k - kb > 0) count += 1;
+    }
+    if (n - K0 - KB > 0) count += 1;
+  }
+  return count;
+}
+
+int check_common(const float* A, float* L, int64_t batch, int64_t n) {
+  if (batch < 0 || n < 0) return CHOL_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0) return CHOL_OK;
+  if (A == nullptr || L == nullptr) return CHOL_ERR_INVALID_ARG;
+  if (n > (int64_t(1) << 20)) return CHOL_ERR_UNSUPPORTED;
+  if (overlaps_partially(A, L, batch * n * n)) return CHOL_ERR_INVALID_ARG;
+  return CHOL_OK;
+}
+
+int potrf_impl(const float* A, float* L, int64_t batch, int64_t n, int* info, void* ws,
+               size_t ws_bytes, cudaStream_t q) {
+  if (n <= 64) return launch_small(A, L, batch, int(n), info, q);
+  if (ws == nullptr || ws_bytes < blocked_workspace(batch, n)) return CHOL_ERR_WORKSPACE;
+  if (batch > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
+  return run_blocked(A, L, batch, n, info, static_cast<float*>(ws), q);
+}
+
+}  // namespace
+
+int prepare_kernels(int /*device*/) { return CHOL_OK; }
+
+}  // namespace chol
+
+using namespace chol;
+
+extern "C" {
+
+int chol_version(void) { return 100; }
+
+const char* chol_strerror(int status) {
+  switch (status) {
+    case CHOL_OK: return "success";
+    case CHOL_ERR_INVALID_ARG: return "invalid argument (shape, null pointer or partial aliasing)";
+    case CHOL_ERR_LAUNCH: return "kernel launch failed";
+    case CHOL_ERR_NOT_SPD: return "matrix is not positive definite (info > 0)";
+    case CHOL_ERR_WAIT_TIMEOUT: return "bounded device-side wait timed out";
+    case CHOL_ERR_WORKSPACE: return "workspace missing or too small";
+    case CHOL_ERR_DEVICE: return "no usable sm_100 CUDA device";
+    case CHOL_ERR_UNSUPPORTED: return "size not supported by this build";
+    default: return "unknown status";
+  }
+}
+
+int chol_prepare(int device) { return prepare_device(device); }
+
+size_t chol_workspace_bytes(int64_t batch, int64_t n) {
+  if (batch <= 0 || n <= 0) return 0;
+  return blocked_workspace(batch, n);
+}
+
+int chol_potrf_batched_ws_f32(const float* A, float* L, int64_t batch, int64_t n, int* info,
+                              void* workspace, size_t workspace_bytes, void* queue) {
+  int st = check_common(A, L, batch, n);
+  if (st || batch == 0 || n == 0) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  return potrf_impl(A, L, batch, n, info, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(queue));
+}
+
+int chol_potrf_batched_f32(const float* A, float* L, int64_t batch, int64_t n, int* info,
+                           void* queue) {
+  int st = check_common(A, L, batch, n);
+  if (st || batch == 0 || n == 0) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  const size_t need = blocked_workspace(batch, n);
+  void* ws = nullptr;
+  if (need) {
+    DeviceState* ds = device_state(dev);
+    std::lock_guard<std::mutex> lock(ds->ws_mu);
+    if (ds->ws_bytes < need) {
+      // Growing: the old buffer may still be read by queued work, so wait for the device.
+      if (ds->ws) {
+        cudaDeviceSynchronize();
+        cudaFree(ds->ws);
+        ds->ws = nullptr;
+        ds->ws_bytes = 0;
+      }
+      if (cudaMalloc(&ds->ws, need) != cudaSuccess) return CHOL_ERR_WORKSPACE;
+      ds->ws_bytes = need;
+    }
+    ws = ds->ws;
+  }
+  return potrf_impl(A, L, batch, n, info, ws, need, static_cast<cudaStream_t>(queue));
+}
+
+int64_t chol_launch_count(int64_t batch, int64_t n) {
+  if (batch <= 0 || n <= 0) return 0;
+  if (n <= 64) return 1;
+  return blocked_launches(n);
+}
+
+int chol_info_check(const int* info, int64_t batch, void* queue, int64_t* first_bad) {
+  if (first_bad) *first_bad = -1;
+  if (batch <= 0) return CHOL_OK;
+  if (info == nullptr) return CHOL_ERR_INVALID_ARG;
+  std::vector<int> h(static_cast<size_t>(batch));
+  cudaStream_t q = static_cast<cudaStream_t>(queue);
+  if (cudaMemcpyAsync(h.data(), info, size_t(batch) * sizeof(int), cudaMemcpyDeviceToHost, q) !=
+      cudaSuccess)
+    return CHOL_ERR_DEVICE;
+  if (cudaStreamSynchronize(q) != cudaSuccess) return CHOL_ERR_DEVICE;
+  for (int64_t m = 0; m < batch; ++m) {
+    if (h[size_t(m)] > 0) {
+      if (first_bad) *first_bad = m;
+      return CHOL_ERR_NOT_SPD;
+    }
+  }
+  return CHOL_OK;
+}
+
+int chol_block_potrf_f32(float* L, int64_t batch, int64_t stride, int64_t ld, int64_t k,
+                         int64_t kb, float* Tinv, int* info, void* queue) {
+  if (L == nullptr || batch < 0 || kb < 1 || kb > kBlock || k < 0 || ld < k + kb)
+    return CHOL_ERR_INVALID_ARG;
+  if (batch == 0) return CHOL_OK;
+  int dev = 0, st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  return launch_potrf_block(L, stride, ld, L, stride, ld, batch, k, kb, Tinv, info,
+                            static_cast<cudaStream_t>(queue), true);
+}
+
+int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t ldc, int64_t m,
+                     int64_t ncols, int64_t K, const float* P, int64_t pstride, int64_t ldp,
+                     const float* Q, int64_t qstride, int64_t ldq, float alpha, float beta,
+                     int64_t diag_offset, int lower_only, void* queue) {
+  if (batch < 0 || m < 0 || ncols < 0 || K < 0) return CHOL_ERR_INVALID_ARG;
+  if (batch == 0 || m == 0 || ncols == 0) return CHOL_OK;
+  if (C == nullptr || (K > 0 && (P == nullptr || Q == nullptr))) return CHOL_ERR_INVALID_ARG;
+  if (ldc < ncols || (K > 0 && (ldp < K || ldq < K))) return CHOL_ERR_INVALID_ARG;
+  if (C == P && (beta != 0.f || ncols > 64)) return CHOL_ERR_INVALID_ARG;
+  int dev = 0, st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  GemmArgs g{};
+  g.C = C;
+  g.cstride = cstride;
+  g.ldc = ldc;
+  g.P = P;
+  g.pstride = pstride;
+  g.ldp = ldp;
+  g.Q = Q;
+  g.qstride = qstride;
+  g.ldq = ldq;
+  g.m = m;
+  g.ncols = ncols;
+  g.K = K;
+  g.alpha = alpha;
+  g.beta = beta;
+  g.diag_offset = diag_offset;
+  g.lower_only = lower_only;
+  g.batch = batch;
+  return launch_gemm_simt(g, static_cast<cudaStream_t>(queue), true);
+}
+
+}  // extern "C"

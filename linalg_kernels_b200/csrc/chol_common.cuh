@@ -1,0 +1,88 @@
+// chol_common.cuh — shared device/host helpers for the sm_100a Cholesky kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/chol_b200.h"
+
+namespace chol {
+
+// ---------------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Every kernel of the blocked schedule starts
+// with griddep_wait() before it touches memory written by the previous kernel on
+// the queue, and calls griddep_launch() once its CTAs are resident, so the next
+// kernel's launch latency overlaps this kernel's tail. Both are no-ops when the
+// kernel was launched without the programmatic-serialization attribute.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------
+// Packed FP32x2 fused multiply-add (sm_100: one instruction, two IEEE fma.rn lanes).
+// d = a * b + c elementwise on (x, y); bitwise identical to two scalar fmaf calls.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t ra, rb, rc, rd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rc) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+  return d;
+}
+
+// Host-side launch helper: cudaLaunchKernelEx with the PDL attribute.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t q, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = q;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+inline int status_from(cudaError_t e) {
+  if (e == cudaSuccess) return CHOL_OK;
+  return CHOL_ERR_LAUNCH;
+}
+
+// Arguments of the NT update/solve GEMM: C = alpha * P * Q^T + beta * C.
+struct GemmArgs {
+  float* C;
+  int64_t cstride, ldc;
+  const float* P;
+  int64_t pstride, ldp;
+  const float* Q;
+  int64_t qstride, ldq;
+  int64_t m, ncols, K;
+  int64_t diag_offset;  // lower_only: write only c <= r + diag_offset
+  float alpha, beta;
+  int lower_only;
+  int64_t batch;
+};
+
+// Host launchers implemented in the .cu files.
+cudaError_t prepare_small();
+int prepare_kernels(int device);
+int launch_small(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q);
+int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaStream_t q,
+                      bool pdl);
+int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, int64_t stride,
+                       int64_t ld, int64_t batch, int64_t k, int64_t kb, float* Tinv, int* info,
+                       cudaStream_t q, bool pdl);
+int launch_gemm_simt(const GemmArgs& g, cudaStream_t q, bool pdl);
+
+}  // namespace chol

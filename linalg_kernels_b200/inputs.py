@@ -1,0 +1,138 @@
+"""Seeded SPD input families for parity tests and benchmarks.
+
+The families are the ones BASELINE.json names for each benchmark shape:
+
+* ``spectral``: A = Q diag(lam) Q^T with Q from the QR of a seeded N(0, 1) matrix and
+  lam log-uniform in [1, lam_max], then symmetrised (A + A^T) / 2. cond(A) <= lam_max.
+* ``covariance``: A = X X^T / n + shift * I with X seeded N(0, 1) of shape (b, n, n).
+  By the Marchenko-Pastur law the spectrum of X X^T / n lies in [0, ~4], so
+  cond(A) <~ (4 + shift) / shift.
+
+plus the structural cases the reference's own harness exercises
+(cholesky/b4096n32/cholesky_b4096n32_modal.py:261-304: diagonal, tridiagonal, low rank,
+row/column scaling, planted spectrum), re-stated here with our own constants. The
+reference's leaderboard generator is not available; these seeded families stand in for
+its inputs at the same shapes.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class Config:
+    name: str
+    batch: int
+    n: int
+    family: str  # "spectral" | "covariance"
+    param: float  # lam_max for spectral, shift for covariance
+    seed: int
+
+
+# BASELINE.json configs; seeds follow the reference's benchmark seeds (AGENTS.md:74-88).
+CONFIGS: dict[str, Config] = {c.name: c for c in [
+    Config("b4096n32", 4096, 32, "spectral", 1e2, 41032),
+    Config("b1024n64", 1024, 64, "spectral", 1e3, 41064),
+    Config("b64n256", 64, 256, "spectral", 1e3, 41256),
+    Config("b640n512", 640, 512, "covariance", 1.0, 510512),
+    Config("b60n1024", 60, 1024, "covariance", 1.0, 511024),
+    Config("b1n16384", 1, 16384, "covariance", 0.5, 48284),
+    Config("b1n32768", 1, 32768, "covariance", 0.5, 48368),
+]}
+
+
+class _NoTF32:
+    """Plain FP32 matmuls (TF32 off) inside the block."""
+
+    def __enter__(self):
+        self._old = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        return self
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self._old
+        return False
+
+
+def _gen(seed: int, device) -> torch.Generator:
+    g = torch.Generator(device=torch.device(device))
+    g.manual_seed(int(seed))
+    return g
+
+
+def spectral(batch: int, n: int, lam_max: float, seed: int, device="cpu"):
+    """Returns (A, cond) with cond the exact per-matrix lam_max/lam_min (float64 tensor)."""
+    g = _gen(seed, device)
+    src = torch.randn(batch, n, n, generator=g, device=device, dtype=torch.float32)
+    q, _ = torch.linalg.qr(src)
+    u = torch.rand(batch, n, generator=g, device=device, dtype=torch.float32)
+    lam = torch.exp(u * math.log(lam_max))
+    with _NoTF32():
+        a = (q * lam.unsqueeze(1)) @ q.transpose(1, 2)
+    a = (a + a.transpose(1, 2)) * 0.5
+    cond = (lam.amax(dim=1) / lam.amin(dim=1)).double()
+    return a.contiguous(), cond
+
+
+def covariance(batch: int, n: int, shift: float, seed: int, device="cpu"):
+    """Returns (A, cond_bound) with the Marchenko-Pastur bound (4.5 + shift) / shift."""
+    g = _gen(seed, device)
+    a = torch.empty(batch, n, n, device=device, dtype=torch.float32)
+    for m in range(batch):  # one matrix at a time keeps the peak memory at 3 matrices
+        x = torch.randn(n, n, generator=g, device=device, dtype=torch.float32)
+        with _NoTF32():
+            torch.matmul(x, x.t(), out=a[m])
+        del x
+        a[m].mul_(1.0 / n)
+        a[m].diagonal().add_(shift)
+    cond = torch.full((batch,), (4.5 + shift) / shift, dtype=torch.float64)
+    return a, cond
+
+
+def config_input(cfg: Config | str, device="cpu", batch: int | None = None):
+    """(A, cond) for a named BASELINE config (optionally with a smaller batch)."""
+    if isinstance(cfg, str):
+        cfg = CONFIGS[cfg]
+    b = cfg.batch if batch is None else batch
+    if cfg.family == "spectral":
+        return spectral(b, cfg.n, cfg.param, cfg.seed, device)
+    return covariance(b, cfg.n, cfg.param, cfg.seed, device)
+
+
+def case(name: str, batch: int, n: int, seed: int, device="cpu") -> torch.Tensor:
+    """Structural SPD cases (float32, contiguous)."""
+    g = _gen(seed, device)
+    eye = torch.eye(n, device=device, dtype=torch.float32).expand(batch, n, n)
+    if name == "diagonal":
+        vals = torch.logspace(0.0, math.log10(7.0), n, device=device)
+        return torch.diag_embed(vals.expand(batch, n)).contiguous()
+    if name == "tridiagonal":
+        d = torch.full((batch, n), 2.5, device=device)
+        e = torch.full((batch, n - 1), -1.0, device=device)
+        return (torch.diag_embed(d) + torch.diag_embed(e, 1) + torch.diag_embed(e, -1)).contiguous()
+    if name == "lowrank":
+        f = torch.randn(batch, n, 3, generator=g, device=device)
+        with _NoTF32():
+            return (f @ f.transpose(1, 2) + 0.25 * eye).contiguous()
+    if name == "spectrum":
+        q, _ = torch.linalg.qr(torch.randn(batch, n, n, generator=g, device=device))
+        vals = torch.logspace(0.0, math.log10(20.0), n, device=device)
+        with _NoTF32():
+            a = (q * vals.view(1, 1, n)) @ q.transpose(1, 2)
+        return ((a + a.transpose(1, 2)) * 0.5).contiguous()
+    x = torch.randn(batch, n, n, generator=g, device=device)
+    with _NoTF32():
+        dense = x @ x.transpose(1, 2) + 3.0 * eye
+    if name == "rowscale":
+        s = torch.logspace(0.0, 0.4, n, device=device).view(1, n)
+        dense = dense * s.unsqueeze(2) * s.unsqueeze(1)
+    elif name != "dense":
+        raise ValueError(f"unknown case {name!r}")
+    return dense.contiguous()
+
+
+CASES = ("dense", "diagonal", "tridiagonal", "lowrank", "spectrum", "rowscale")

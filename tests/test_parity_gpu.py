@@ -1,0 +1,199 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the reference's outputs.
+
+Small cases: elementwise against tests/golden (the reference's own custom_kernel output,
+LAPACK SPOTRF) and against the CPU oracle, with the north-star tolerances
+(||L L^T - A||_F / ||A||_F <= 1e-5, max|L - L_ref| <= cond(A) n eps32 max|L_ref|) plus the
+reference harness's property gate. BASELINE.json sizes: the same bounds against the
+reference path run on the GPU (torch.linalg.cholesky_ex, i.e. submission.py:7 on CUDA)
+and size-independent properties (exact-zero upper, positive diagonal, residual,
+determinism, input untouched).
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from linalg_kernels_b200 import _lib, inputs
+from linalg_kernels_b200.cholesky import cholesky, cholesky_ex, custom_kernel
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _names(golden):
+    return [str(n) for n in golden["_names"]]
+
+
+def _gpu_factor(a_np):
+    a = torch.from_numpy(np.ascontiguousarray(a_np)).to(DEV)
+    l = custom_kernel(a)
+    torch.cuda.synchronize()
+    return l.cpu().numpy()
+
+
+def test_golden_cases_match_reference(golden):
+    for name in _names(golden):
+        a, l_ref, cond = golden[f"{name}/A"], golden[f"{name}/L"], golden[f"{name}/cond"]
+        l = _gpu_factor(a)
+        res = oracle.check_factor(a, l, l_ref=l_ref, cond=cond)
+        assert res["ok"], (name, res)
+        l_or, _ = oracle.potrf(a)
+        res2 = oracle.check_factor(a, l, l_ref=l_or, cond=cond)
+        assert res2["ok"], (name, "vs oracle", res2)
+
+
+def test_not_spd_info_matches_reference(golden):
+    for name in [str(n) for n in golden["_notspd"]]:
+        a = torch.from_numpy(golden[f"{name}/A"]).to(DEV)
+        _, info = cholesky_ex(a)
+        np.testing.assert_array_equal(info.cpu().numpy(), golden[f"{name}/info"], err_msg=name)
+        with pytest.raises(torch.linalg.LinAlgError):
+            cholesky(a)
+
+
+def test_lower_triangle_only(golden):
+    a = golden["upper_garbage_b2n40/A"]
+    np.testing.assert_array_equal(_gpu_factor(a), _gpu_factor(np.tril(a)))
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 4, 5, 8, 9, 15, 16, 17, 24, 31, 32, 33, 48, 63, 64, 65,
+                               96, 100, 127, 128, 129, 191, 200, 255, 256, 257, 300])
+@pytest.mark.parametrize("batch", [1, 7])
+def test_sizes_against_oracle(n, batch):
+    a, cond = inputs.spectral(batch, n, 100.0, 1000 * n + batch)
+    a = a.numpy()
+    l = _gpu_factor(a)
+    l_or, info = oracle.potrf(a)
+    assert (info == 0).all()
+    res = oracle.check_factor(a, l, l_ref=l_or, cond=cond.numpy())
+    assert res["ok"], (n, batch, res)
+
+
+@pytest.mark.parametrize("name", ["dense", "diagonal", "tridiagonal", "lowrank", "spectrum",
+                                  "rowscale"])
+@pytest.mark.parametrize("n", [32, 64, 128, 256, 512])
+def test_case_families(name, n):
+    a = inputs.case(name, 2, n, 77 + n)
+    ev = torch.linalg.eigvalsh(a.double())
+    cond = (ev[:, -1] / ev[:, 0]).numpy()
+    a = a.numpy()
+    l = _gpu_factor(a)
+    l_or, _ = oracle.potrf(a)
+    res = oracle.check_factor(a, l, l_ref=l_or, cond=cond)
+    assert res["ok"], (name, n, res)
+
+
+def test_diagonal_known_answer():
+    d = torch.logspace(-2, 2, 96)
+    a = torch.diag_embed(d.expand(3, 96)).contiguous()
+    l = custom_kernel(a.to(DEV)).cpu()
+    want = torch.diag_embed(torch.sqrt(d).expand(3, 96))
+    assert (l - want).abs().max().item() <= 2e-7 * 10.0
+
+
+def _check_full_config(name, batch=None):
+    cfg = inputs.CONFIGS[name]
+    a, cond = inputs.config_input(cfg, device=DEV, batch=batch)
+    a_before = a.clone()
+    l = custom_kernel(a)
+    l_ref = torch.linalg.cholesky_ex(a, check_errors=False).L  # the reference path on GPU
+    torch.cuda.synchronize()
+    assert torch.equal(a, a_before), "input was modified"
+    n = cfg.n
+    assert torch.isfinite(l).all()
+    assert (torch.triu(l, 1) == 0).all()
+    assert (l.diagonal(dim1=-2, dim2=-1) > 0).all()
+    # residual in float64 on the device, lower triangle of A
+    a64 = torch.tril(a.double())
+    a64 = a64 + torch.tril(a64, -1).transpose(-1, -2)
+    l64 = l.double()
+    rel = torch.linalg.matrix_norm(l64 @ l64.transpose(-1, -2) - a64) / torch.linalg.matrix_norm(a64)
+    assert rel.max().item() <= oracle.REL_RESIDUAL_TOL, rel.max().item()
+    diff = (l - l_ref).abs().reshape(l.shape[0], -1).amax(dim=1).double().cpu()
+    bound = cond.reshape(-1) * n * oracle.EPS32 * l_ref.abs().reshape(l.shape[0], -1).amax(dim=1).double().cpu()
+    assert (diff <= bound).all(), (diff.max().item(), bound.min().item())
+    l2 = custom_kernel(a)
+    assert torch.equal(l, l2), "not deterministic"
+    return rel.max().item()
+
+
+@pytest.mark.parametrize("name", ["b4096n32", "b1024n64", "b64n256", "b640n512", "b60n1024"])
+def test_baseline_configs_full_size(name):
+    _check_full_config(name)
+
+
+def test_baseline_config_n16384():
+    _check_full_config("b1n16384")
+
+
+def test_non_contiguous_input():
+    a, _ = inputs.spectral(4, 48, 10.0, 3)
+    big = torch.zeros(4, 48, 96)
+    big[:, :, ::2] = a
+    x = big[:, :, ::2].to(DEV)
+    assert not x.is_contiguous()
+    l = custom_kernel(x).cpu().numpy()
+    l_or, _ = oracle.potrf(a.numpy())
+    assert oracle.check_factor(a.numpy(), l, l_ref=l_or, cond=np.full(4, 10.0))["ok"]
+
+
+def test_leading_batch_dims_and_2d():
+    a, _ = inputs.spectral(6, 40, 10.0, 4)
+    l = custom_kernel(a.reshape(2, 3, 40, 40).to(DEV))
+    assert l.shape == (2, 3, 40, 40)
+    l2 = custom_kernel(a[0].to(DEV))
+    assert l2.shape == (40, 40)
+    assert torch.equal(l.reshape(6, 40, 40)[0], l2)
+
+
+def _abi_call(a, l, batch, n):
+    lib = _lib.load()
+    return lib.chol_potrf_batched_f32(ctypes.c_void_p(a), ctypes.c_void_p(l), batch, n, None,
+                                      ctypes.c_void_p(_lib.current_queue(torch.device(DEV))))
+
+
+@pytest.mark.parametrize("n", [32, 64, 200])
+def test_abi_in_place_and_canaries(n):
+    """Library-managed workspace entry point; A == L in place; canaries around L."""
+    a, cond = inputs.spectral(3, n, 50.0, 11 + n)
+    want = custom_kernel(a.to(DEV))
+    pad = 64
+    buf = torch.full((3 * n * n + 2 * pad,), 12345.0, device=DEV)
+    buf[pad:pad + 3 * n * n] = a.reshape(-1).to(DEV)
+    base = buf.data_ptr() + pad * 4
+    assert _abi_call(base, base, 3, n) == _lib.CHOL_OK
+    torch.cuda.synchronize()
+    assert (buf[:pad] == 12345.0).all() and (buf[-pad:] == 12345.0).all()
+    got = buf[pad:pad + 3 * n * n].reshape(3, n, n)
+    assert torch.equal(got, want)
+
+
+def test_building_blocks_against_torch():
+    """chol_block_potrf_f32 + chol_gemm_nt_f32 reproduce one blocked step."""
+    lib = _lib.load()
+    n, kb = 160, 64
+    a, _ = inputs.spectral(2, n, 20.0, 5)
+    l = torch.tril(a).to(DEV).contiguous()
+    tinv = torch.zeros(2, 64, 64, device=DEV)
+    q = ctypes.c_void_p(_lib.current_queue(torch.device(DEV)))
+    assert lib.chol_block_potrf_f32(ctypes.c_void_p(l.data_ptr()), 2, n * n, n, 0, kb,
+                                    ctypes.c_void_p(tinv.data_ptr()), None, q) == 0
+    l11 = l[:, :kb, :kb]
+    ref11 = torch.linalg.cholesky(a[:, :kb, :kb].to(DEV).double()).float()
+    assert (l11 - ref11).abs().max().item() < 1e-5
+    eye = torch.eye(kb, device=DEV)
+    assert (tinv @ l11 - eye).abs().max().item() < 1e-4
+    # panel solve in place: X = A21 * T^T
+    x = l[:, kb:, :kb]
+    want_x = a[:, kb:, :kb].to(DEV) @ tinv.transpose(1, 2)
+    st = lib.chol_gemm_nt_f32(ctypes.c_void_p(x.data_ptr()), 2, n * n, n, n - kb, kb, kb,
+                              ctypes.c_void_p(x.data_ptr()), n * n, n,
+                              ctypes.c_void_p(tinv.data_ptr()), 64 * 64, 64,
+                              1.0, 0.0, 0, 0, q)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert (l[:, kb:, :kb] - want_x).abs().max().item() < 1e-4

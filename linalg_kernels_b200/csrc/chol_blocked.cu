@@ -104,22 +104,20 @@ __global__ void __launch_bounds__(128)
   }
   __syncthreads();
 
-  int fail = 0;
   if (tid < 32) {
-    float a[2][64];
+    float2 a[2][32];
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       const float* rp = tile + (s * 32 + tid) * kPBLD;
 #pragma unroll
       for (int q = 0; q < (s + 1) * 8; ++q) {
         const float4 v = *reinterpret_cast<const float4*>(rp + 4 * q);
-        a[s][4 * q + 0] = v.x;
-        a[s][4 * q + 1] = v.y;
-        a[s][4 * q + 2] = v.z;
-        a[s][4 * q + 3] = v.w;
+        a[s][2 * q] = make_float2(v.x, v.y);
+        a[s][2 * q + 1] = make_float2(v.z, v.w);
       }
     }
-    warp_potrf_rows<64>(a, col, tid, fail);
+    warp_potrf_rows<64>(a, col, tid);
+    __syncwarp();
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       const int i = s * 32 + tid;
@@ -128,17 +126,24 @@ __global__ void __launch_bounds__(128)
       for (int q = 0; q < kPB / 4; ++q) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (4 * q < (s + 1) * 32) {
-          v.x = (4 * q + 0 <= i) ? a[s][4 * q + 0] : 0.f;
-          v.y = (4 * q + 1 <= i) ? a[s][4 * q + 1] : 0.f;
-          v.z = (4 * q + 2 <= i) ? a[s][4 * q + 2] : 0.f;
-          v.w = (4 * q + 3 <= i) ? a[s][4 * q + 3] : 0.f;
+          const float2 lo = a[s][2 * q], hi = a[s][2 * q + 1];
+          v.x = (4 * q + 0 <= i) ? lo.x : 0.f;
+          v.y = (4 * q + 1 <= i) ? lo.y : 0.f;
+          v.z = (4 * q + 2 <= i) ? hi.x : 0.f;
+          v.w = (4 * q + 3 <= i) ? hi.y : 0.f;
         }
         *reinterpret_cast<float4*>(rp + 4 * q) = v;
       }
     }
     __syncwarp();
-    rdiag[tid] = __frcp_rn(tile[tid * kPBLD + tid]);
-    rdiag[tid + 32] = __frcp_rn(tile[(tid + 32) * kPBLD + tid + 32]);
+    const float d0 = tile[tid * kPBLD + tid];
+    const float d1 = tile[(tid + 32) * kPBLD + tid + 32];
+    rdiag[tid] = __frcp_rn(d0);
+    rdiag[tid + 32] = __frcp_rn(d1);
+    // first row whose diagonal is not > 0 (NaN included) is the first failing column
+    const unsigned b0 = __ballot_sync(0xffffffffu, !(d0 > 0.f));
+    const unsigned b1 = __ballot_sync(0xffffffffu, !(d1 > 0.f));
+    const int fail = b0 ? __ffs(b0) : (b1 ? 32 + __ffs(b1) : 0);
     if (tid == 0 && info != nullptr) {
       const int f = (fail > kb) ? 0 : fail;
       if (k == 0)

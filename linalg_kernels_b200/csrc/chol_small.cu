@@ -26,7 +26,7 @@ constexpr size_t small_smem_bytes() {
 // FULL: n == NP and 16-byte aligned rows (vector path). Otherwise scalar loads with
 // identity padding of rows/columns n..NP-1.
 template <int NP, bool FULL>
-__global__ void __launch_bounds__(kSmallWarps * 32)
+__global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 8 : 1)
     small_potrf_kernel(const float* __restrict__ A, float* __restrict__ L, int64_t batch, int n,
                        int* __restrict__ info) {
   constexpr int LPM = WarpShape<NP>::LPM;
@@ -58,21 +58,19 @@ __global__ void __launch_bounds__(kSmallWarps * 32)
     if (m < batch) {
       const float* src = A + m * int64_t(n) * n;
       if (FULL) {
+        // 16-byte chunks that hold at least one lower-triangle element, all in flight
         constexpr int C4 = NP / 4;
 #pragma unroll
         for (int idx = lane; idx < NP * C4; idx += 32) {
           const int r = idx / C4, c4 = idx % C4;
-          if (c4 * 4 <= r) {
-            const float4 v = __ldcs(reinterpret_cast<const float4*>(src + r * NP + c4 * 4));
-            *reinterpret_cast<float4*>(st + r * LDS + c4 * 4) = v;
-          }
+          if (c4 * 4 <= r) cp_async16(st + r * LDS + c4 * 4, src + r * NP + c4 * 4);
         }
         rpad = NP;
       } else {
         const int nn = n * n;
         for (int idx = lane; idx < nn; idx += 32) {
           const int r = idx / n, c = idx - r * n;
-          if (c <= r) st[r * LDS + c] = __ldcs(src + idx);
+          if (c <= r) cp_async4(st + r * LDS + c, src + idx);
         }
         rpad = n;
       }
@@ -83,10 +81,11 @@ __global__ void __launch_bounds__(kSmallWarps * 32)
       st[r * LDS + c] = (r == c) ? 1.f : 0.f;
     }
   }
+  cp_async_wait_all();
   __syncwarp();
 
-  // ---- rows to registers ----
-  float a[R][NP];
+  // ---- rows to registers (column pairs) ----
+  float2 a[R][NP / 2];
   const float* mst = stage + grp * TILE;
 #pragma unroll
   for (int s = 0; s < R; ++s) {
@@ -94,54 +93,70 @@ __global__ void __launch_bounds__(kSmallWarps * 32)
 #pragma unroll
     for (int q = 0; q < (s + 1) * LPM / 4; ++q) {
       const float4 v = *reinterpret_cast<const float4*>(rp + 4 * q);
-      a[s][4 * q + 0] = v.x;
-      a[s][4 * q + 1] = v.y;
-      a[s][4 * q + 2] = v.z;
-      a[s][4 * q + 3] = v.w;
+      a[s][2 * q] = make_float2(v.x, v.y);
+      a[s][2 * q + 1] = make_float2(v.z, v.w);
     }
   }
 
-  int fail = 0;
-  warp_potrf_rows<NP>(a, col, gl, fail);
+  warp_potrf_rows<NP>(a, col, gl);
   __syncwarp();
 
   // ---- registers to staging, strict upper part as exact zeros ----
+  // A non-positive (or NaN) pivot in column j makes L[j][j] NaN or non-positive and every
+  // later pivot NaN, so the first row whose diagonal is not > 0 is LAPACK's info - 1.
+  bool bad[R];
 #pragma unroll
   for (int s = 0; s < R; ++s) {
     const int i = s * LPM + gl;
     float* rp = stage + grp * TILE + i * LDS;
+    bad[s] = false;
 #pragma unroll
     for (int q = 0; q < NP / 4; ++q) {
-      float4 v;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (4 * q < (s + 1) * LPM) {
-        v.x = (4 * q + 0 <= i) ? a[s][4 * q + 0] : 0.f;
-        v.y = (4 * q + 1 <= i) ? a[s][4 * q + 1] : 0.f;
-        v.z = (4 * q + 2 <= i) ? a[s][4 * q + 2] : 0.f;
-        v.w = (4 * q + 3 <= i) ? a[s][4 * q + 3] : 0.f;
-      } else {
-        v = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float2 lo = a[s][2 * q], hi = a[s][2 * q + 1];
+        v.x = (4 * q + 0 <= i) ? lo.x : 0.f;
+        v.y = (4 * q + 1 <= i) ? lo.y : 0.f;
+        v.z = (4 * q + 2 <= i) ? hi.x : 0.f;
+        v.w = (4 * q + 3 <= i) ? hi.y : 0.f;
+        if (4 * q <= i && i < 4 * q + 4) {
+          const float dg = (i & 2) ? ((i & 1) ? hi.y : hi.x) : ((i & 1) ? lo.y : lo.x);
+          bad[s] = !(dg > 0.f);
+        }
       }
       *reinterpret_cast<float4*>(rp + 4 * q) = v;
     }
   }
+  int fail = 0;
+#pragma unroll
+  for (int s = R - 1; s >= 0; --s) {
+    const unsigned bits = (__ballot_sync(0xffffffffu, bad[s]) >> (grp * LPM)) &
+                          (LPM == 32 ? 0xffffffffu : ((1u << LPM) - 1u));
+    if (bits) fail = s * LPM + __ffs(bits);  // 1-based row of the first failure in slot s
+  }
   __syncwarp();
 
-  // ---- store: full rows, coalesced ----
+  // ---- store: full rows. Vector path: one bulk async copy per row, issued by the lane
+  // that holds the row; scalar path: coalesced 4-byte stores. ----
+  if (FULL) {
+    fence_proxy_async_smem();
+    __syncwarp();
 #pragma unroll 1
-  for (int mm = 0; mm < MPW; ++mm) {
-    const int64_t m = mbase + mm;
-    if (m >= batch) break;
-    const float* st = stage + mm * TILE;
-    float* dst = L + m * int64_t(n) * n;
-    if (FULL) {
-      constexpr int C4 = NP / 4;
-#pragma unroll
-      for (int idx = lane; idx < NP * C4; idx += 32) {
-        const int r = idx / C4, c4 = idx % C4;
-        __stcs(reinterpret_cast<float4*>(dst + r * NP + c4 * 4),
-               *reinterpret_cast<const float4*>(st + r * LDS + c4 * 4));
-      }
-    } else {
+    for (int mm = 0; mm < MPW; ++mm) {
+      const int64_t m = mbase + mm;
+      if (m >= batch) break;
+      const float* st = stage + mm * TILE;
+      float* dst = L + m * int64_t(NP) * NP;
+      for (int r = lane; r < NP; r += 32) bulk_store(dst + r * NP, st + r * LDS, NP * 4);
+    }
+    bulk_store_wait_read();
+  } else {
+#pragma unroll 1
+    for (int mm = 0; mm < MPW; ++mm) {
+      const int64_t m = mbase + mm;
+      if (m >= batch) break;
+      const float* st = stage + mm * TILE;
+      float* dst = L + m * int64_t(n) * n;
       const int nn = n * n;
       for (int idx = lane; idx < nn; idx += 32) {
         const int r = idx / n, c = idx - r * n;

@@ -114,7 +114,7 @@ def _check_full_config(name, batch=None):
     rel = torch.linalg.matrix_norm(l64 @ l64.transpose(-1, -2) - a64) / torch.linalg.matrix_norm(a64)
     assert rel.max().item() <= oracle.REL_RESIDUAL_TOL, rel.max().item()
     diff = (l - l_ref).abs().reshape(l.shape[0], -1).amax(dim=1).double().cpu()
-    bound = cond.reshape(-1) * n * oracle.EPS32 * l_ref.abs().reshape(l.shape[0], -1).amax(dim=1).double().cpu()
+    bound = cond.reshape(-1).cpu() * n * oracle.EPS32 * l_ref.abs().reshape(l.shape[0], -1).amax(dim=1).double().cpu()
     assert (diff <= bound).all(), (diff.max().item(), bound.min().item())
     l2 = custom_kernel(a)
     assert torch.equal(l, l2), "not deterministic"
@@ -132,9 +132,9 @@ def test_baseline_config_n16384():
 
 def test_non_contiguous_input():
     a, _ = inputs.spectral(4, 48, 10.0, 3)
-    big = torch.zeros(4, 48, 96)
-    big[:, :, ::2] = a
-    x = big[:, :, ::2].to(DEV)
+    big = torch.zeros(4, 48, 96, device=DEV)
+    big[:, :, ::2] = a.to(DEV)
+    x = big[:, :, ::2]
     assert not x.is_contiguous()
     l = custom_kernel(x).cpu().numpy()
     l_or, _ = oracle.potrf(a.numpy())

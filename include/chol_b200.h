@@ -104,6 +104,22 @@ CHOL_API int chol_potrf_batched_ws_f32(const float* A, float* L, int64_t batch, 
 CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
 
 /*
+ * Library options (process-wide, for tests and benchmarks):
+ *   CHOL_OPT_GEMM_ENGINE: 0 = auto (tcgen05 3xTF32 tensor cores where the operands allow
+ *   TMA, FP32 FMA otherwise; default), 1 = FP32 FMA only, 2 = tensor cores only.
+ */
+#define CHOL_OPT_GEMM_ENGINE 1
+CHOL_API int chol_set_option(int option, int value);
+
+/*
+ * Synchronises the queue, then reads and clears the device status word that the kernels'
+ * bounded waits write on expiry. Returns CHOL_OK, CHOL_ERR_WAIT_TIMEOUT or
+ * CHOL_ERR_DEVICE. (The reference's flag waits have no bound and no status,
+ * cholesky/cholesky.py:3588-3598, 4846-4853.)
+ */
+CHOL_API int chol_status_check(void* queue);
+
+/*
  * Host-side helper: copies info (batch ints, device) to the host after synchronising
  * the queue and returns CHOL_ERR_NOT_SPD if any entry is > 0 (first failing matrix in
  * *first_bad, or -1). torch.linalg.cholesky (check_errors=True) behaviour; the

@@ -24,6 +24,9 @@ CHOL_ERR_WORKSPACE = 5
 CHOL_ERR_DEVICE = 6
 CHOL_ERR_UNSUPPORTED = 7
 
+CHOL_OPT_GEMM_ENGINE = 1
+ENGINE_AUTO, ENGINE_FMA, ENGINE_TENSOR = 0, 1, 2
+
 _i64 = ctypes.c_int64
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
@@ -39,6 +42,8 @@ SIGNATURES: dict[str, tuple] = {
     "chol_potrf_batched_f32": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "chol_potrf_batched_ws_f32": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
     "chol_launch_count": (_i64, [_i64, _i64]),
+    "chol_set_option": (_int, [_int, _int]),
+    "chol_status_check": (_int, [_vp]),
     "chol_info_check": (_int, [_vp, _i64, _vp, ctypes.POINTER(_i64)]),
     "chol_block_potrf_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "chol_gemm_nt_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64,

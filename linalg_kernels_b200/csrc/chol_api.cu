@@ -114,7 +114,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       s.beta = 0.f;
       s.lower_only = 0;
       s.batch = batch;
-      st = launch_gemm_simt(s, q, true);
+      st = launch_gemm(s, q, true);
       if (st) return st;
       const int64_t inpanel = K0 + KB - k - kb;
       if (inpanel > 0) {
@@ -136,7 +136,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
         u.diag_offset = 0;
         u.lower_only = 1;
         u.batch = batch;
-        st = launch_gemm_simt(u, q, true);
+        st = launch_gemm(u, q, true);
         if (st) return st;
       }
     }
@@ -160,7 +160,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       t.diag_offset = 0;
       t.lower_only = 1;
       t.batch = batch;
-      st = launch_gemm_simt(t, q, true);
+      st = launch_gemm(t, q, true);
       if (st) return st;
     }
   }
@@ -204,7 +204,19 @@ int potrf_impl(const float* A, float* L, int64_t batch, int64_t n, int* info, vo
 
 }  // namespace
 
-int prepare_kernels(int /*device*/) { return CHOL_OK; }
+int prepare_kernels(int /*device*/) {
+  return prepare_tc() == cudaSuccess ? CHOL_OK : CHOL_ERR_DEVICE;
+}
+
+int g_gemm_engine = 0;
+
+int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl) {
+  if (g.m <= 0 || g.ncols <= 0) return CHOL_OK;
+  const bool tc = tc_supported(g);
+  if (g_gemm_engine == 2 && !tc) return CHOL_ERR_UNSUPPORTED;
+  if (g_gemm_engine != 1 && tc) return launch_gemm_tc(g, q, pdl, nullptr);
+  return launch_gemm_simt(g, q, pdl);
+}
 
 }  // namespace chol
 
@@ -280,6 +292,24 @@ int64_t chol_launch_count(int64_t batch, int64_t n) {
   return blocked_launches(n);
 }
 
+int chol_set_option(int option, int value) {
+  if (option == CHOL_OPT_GEMM_ENGINE) {
+    if (value < 0 || value > 2) return CHOL_ERR_INVALID_ARG;
+    g_gemm_engine = value;
+    return CHOL_OK;
+  }
+  return CHOL_ERR_INVALID_ARG;
+}
+
+int chol_status_check(void* queue) {
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(queue)) != cudaSuccess)
+    return CHOL_ERR_DEVICE;
+  int v = 0;
+  int st = read_and_clear_status(&v);
+  if (st) return st;
+  return v ? v : CHOL_OK;
+}
+
 int chol_info_check(const int* info, int64_t batch, void* queue, int64_t* first_bad) {
   if (first_bad) *first_bad = -1;
   if (batch <= 0) return CHOL_OK;
@@ -341,7 +371,7 @@ int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t ldc, int6
   g.diag_offset = diag_offset;
   g.lower_only = lower_only;
   g.batch = batch;
-  return launch_gemm_simt(g, static_cast<cudaStream_t>(queue), true);
+  return launch_gemm(g, static_cast<cudaStream_t>(queue), true);
 }
 
 }  // extern "C"

@@ -92,16 +92,20 @@ __global__ void __launch_bounds__(128)
   griddep_wait();
   griddep_launch();
 
-  // load lower part of the block; identity outside kb
+  // load the block: every 4-byte element of the lower part in flight at once (cp.async),
+  // identity outside kb, zeros above the diagonal
   for (int idx = tid; idx < kPB * kPB; idx += 128) {
     const int r = idx / kPB, c = idx % kPB;
-    float v;
-    if (r < kb && c < kb)
-      v = (c <= r) ? src[r * lds + c] : 0.f;
-    else
-      v = (r == c) ? 1.f : 0.f;
-    tile[r * kPBLD + c] = v;
+    if (r < kb && c < kb) {
+      if (c <= r)
+        cp_async4(&tile[r * kPBLD + c], src + r * lds + c);
+      else
+        tile[r * kPBLD + c] = 0.f;
+    } else {
+      tile[r * kPBLD + c] = (r == c) ? 1.f : 0.f;
+    }
   }
+  cp_async_wait_all();
   __syncthreads();
 
   if (tid < 32) {

@@ -120,5 +120,13 @@ int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, i
                        int64_t ld, int64_t batch, int64_t k, int64_t kb, float* Tinv, int* info,
                        cudaStream_t q, bool pdl);
 int launch_gemm_simt(const GemmArgs& g, cudaStream_t q, bool pdl);
+bool tc_supported(const GemmArgs& g);
+int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status);
+cudaError_t prepare_tc();
+int read_and_clear_status(int* out);
+// Engine choice for the NT-GEMM: 0 auto (tensor cores when the operands allow TMA), 1 FP32
+// FMA only, 2 tensor cores only (CHOL_ERR_UNSUPPORTED where TMA cannot be used).
+extern int g_gemm_engine;
+int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl);
 
 }  // namespace chol

@@ -1,0 +1,573 @@
+// chol_tc.cu — tensor-core (tcgen05 / TMEM / TMA) NT-GEMM with a 3xTF32 split, the
+// trailing-update and panel-solve engine of the blocked path.
+//
+//   C[r][c] = alpha * sum_q P[r][q] Q[c][q] + beta * C[r][c]     (lower tiles optional)
+//
+// FP32 accuracy from TF32 tensor cores: every operand x is split into hi = x with its low
+// 13 mantissa bits cleared (exactly representable in TF32) and lo = x - hi (exact in
+// FP32; its TF32 truncation loses < 2^-21 |x|), and the product is accumulated as
+//   P_hi Q_hi + P_hi Q_lo + P_lo Q_hi            (the lo*lo term, < 2^-22 |P||Q|, dropped)
+// in one FP32 TMEM accumulator. Plain TF32 (the reference's cuBLAS FAST_TF32 GEMMs,
+// cholesky/cholesky.py:2529-2553, 5625-5690) has ~1e-3 relative error per product, which
+// fails a 1e-5 residual; 3xTF32 keeps the factor at FP32 accuracy.
+//
+// One CTA computes one BM x BN tile (BM = 128 rows of P, BN = 64/128/256 rows of Q):
+//   warp 0      TMA producer: 128B-swizzled K-major boxes of P and Q (32 floats = 128 B
+//               of K per row) into a STAGES-deep ring, mbarrier complete_tx.
+//   warp 1      TMEM allocator; one elected thread issues tcgen05.mma kind::tf32
+//               (M128 x N x K8, 3 per K8 step) and tcgen05.commit to release stages.
+//   warps 2..5  split each landed stage into hi (in place) and lo (second buffer), then
+//               the epilogue: tcgen05.ld 32x32b rows of the accumulator, combine with C,
+//               write back (rows of a warp = its TMEM lane quarter).
+// Every mbarrier wait is bounded by %globaltimer (2 s); on expiry the kernel records
+// CHOL_ERR_WAIT_TIMEOUT in the device status word, skips the remaining work, frees its
+// TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "chol_common.cuh"
+
+namespace chol {
+
+__device__ int g_device_status = 0;
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 32;  // fp32 elements of K per stage = one 128-byte swizzle row
+constexpr int kThreads = 320;  // producer, MMA, 4 converter warps, 4 epilogue warps
+
+template <int BN>
+struct TcCfg {
+  static constexpr int STAGES = BN >= 256 ? 2 : (BN == 128 ? 3 : 4);
+  static constexpr int A_BYTES = kBM * kBK * 4;
+  static constexpr int B_BYTES = BN * kBK * 4;
+  static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr int TMEM_COLS = BN;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+  // TMEM: two BN-column FP32 accumulators (double buffer), 2*BN <= 512
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+};
+
+// ------------------------------- PTX wrappers ---------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Bounded wait for the completion of phase `parity`. Returns false (and records the
+// timeout in the status word) if it does not complete within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
+      atomicExch(status, CHOL_ERR_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(const void* smem_tile) {
+  const uint32_t addr = smem_u32(smem_tile);
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3FFF);  // start address
+  d |= uint64_t(1) << 16;               // leading byte offset (unused for SW128 K-major)
+  d |= uint64_t(1024 >> 4) << 32;       // stride byte offset: 8 rows x 128 B
+  d |= uint64_t(1) << 46;               // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;               // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, K-major both, N, M = 128.
+template <int BN>
+__device__ __forceinline__ uint32_t tf32_idesc() {
+  return (1u << 4)                       // D format f32
+         | (2u << 7)                     // A format tf32
+         | (2u << 10)                    // B format tf32
+         | (uint32_t(BN >> 3) << 17)     // N >> 3
+         | (uint32_t(kBM >> 4) << 24);   // M >> 4
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// hi/lo split of one 16-byte chunk: lo to the twin buffer; hi written back in place when
+// WRITE_HI (otherwise the tensor core's own TF32 conversion of x must equal hi).
+template <bool WRITE_HI>
+__device__ __forceinline__ void split4(float4* hi_p, float4* lo_p) {
+  const float4 x = *hi_p;
+  float4 h, l;
+  h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+  h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+  h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+  h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+  l.x = x.x - h.x;
+  l.y = x.y - h.y;
+  l.z = x.z - h.z;
+  l.w = x.w - h.w;
+  if (WRITE_HI) *hi_p = h;
+  *lo_p = l;
+}
+
+// Tile enumeration: per matrix, row tiles tm = 0..TM-1 and, in row tm, column tiles
+// tn = 0..last(tm) where last(tm) = TN-1 for a full GEMM and the last tile touching the
+// lower part (c <= r + diag_offset) otherwise. Tiles of one matrix are numbered row by row.
+struct TileSpace {
+  int64_t tiles_m, tiles_n, per_matrix, total;
+  int64_t diag_offset;
+  int lower_only;
+  int bn;
+  __device__ __forceinline__ int64_t row_count(int64_t tm) const {
+    if (!lower_only) return tiles_n;
+    const int64_t last_c = tm * kBM + kBM - 1 + diag_offset;
+    if (last_c < 0) return 0;
+    const int64_t cnt = last_c / bn + 1;
+    return cnt < tiles_n ? cnt : tiles_n;
+  }
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                   GemmArgs g, TileSpace ts, int* status) {
+  using Cfg = TcCfg<BN>;
+  constexpr int S = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+
+  griddep_wait();  // before anything else: keeps the PDL chain ordered
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  auto stA = [&](int s) { return reinterpret_cast<float*>(smem + size_t(s) * Cfg::STAGE_BYTES); };
+  auto stAlo = [&](int s) { return stA(s) + Cfg::A_BYTES / 4; };
+  auto stB = [&](int s) { return stAlo(s) + Cfg::A_BYTES / 4; };
+  auto stBlo = [&](int s) { return stB(s) + Cfg::B_BYTES / 4; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(S) * Cfg::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* conv = bars + S;
+  uint64_t* empty = bars + 2 * S;
+  uint64_t* tfull = bars + 3 * S;       // [2] accumulator ready
+  uint64_t* tempty = bars + 3 * S + 2;  // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
+  int* st_word = status ? status : &g_device_status;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&tmP);
+    prefetch_map(&tmQ);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(uint32_t(2 * Cfg::TMEM_COLS))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  griddep_launch();
+  const uint32_t tmem = *tmem_slot;
+  const int num_k = int((g.K + kBK - 1) / kBK);
+
+  // This CTA's tiles: t = blockIdx.x, blockIdx.x + gridDim.x, ...  Walk (matrix, tm, tn).
+  struct Cursor {
+    int64_t t, mi, tm, tn, row_base;  // row_base: index of tile (mi, tm, 0) within matrix
+    bool valid;
+  };
+  auto first_tile = [&](Cursor& c) {
+    c.t = blockIdx.x;
+    c.valid = c.t < ts.total;
+    if (!c.valid) return;
+    c.mi = c.t / ts.per_matrix;
+    int64_t r = c.t - c.mi * ts.per_matrix;
+    c.tm = 0;
+    c.row_base = 0;
+    for (;;) {
+      const int64_t cnt = ts.row_count(c.tm);
+      if (r < cnt) break;
+      r -= cnt;
+      c.row_base += cnt;
+      ++c.tm;
+    }
+    c.tn = r;
+  };
+  auto next_tile = [&](Cursor& c) {
+    c.t += gridDim.x;
+    c.valid = c.t < ts.total;
+    if (!c.valid) return;
+    const int64_t mi = c.t / ts.per_matrix;
+    int64_t r = c.t - mi * ts.per_matrix;
+    if (mi != c.mi) {
+      c.mi = mi;
+      c.tm = 0;
+      c.row_base = 0;
+    }
+    r -= c.row_base;
+    for (;;) {
+      const int64_t cnt = ts.row_count(c.tm);
+      if (r < cnt) break;
+      r -= cnt;
+      c.row_base += cnt;
+      ++c.tm;
+    }
+    c.tn = r;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      Cursor c;
+      first_tile(c);
+      uint32_t kt = 0;
+      bool ok = true;
+      for (; c.valid && ok; next_tile(c)) {
+        const int zc = int(c.mi);
+        const int y0 = int(c.tm * kBM), y1 = int(c.tn * BN);
+        for (int k = 0; k < num_k; ++k, ++kt) {
+          const int s = int(kt % S);
+          const uint32_t ph = (kt / S) & 1u;
+          if (kt >= uint32_t(S) && !mbar_wait(&empty[s], ph ^ 1u, st_word)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], Cfg::A_BYTES + Cfg::B_BYTES);
+          tma_load_3d(stA(s), &tmP, k * kBK, y0, zc, &full[s]);
+          tma_load_3d(stB(s), &tmQ, k * kBK, y1, zc, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = tf32_idesc<BN>();
+      Cursor c;
+      first_tile(c);
+      uint32_t kt = 0, it = 0;
+      bool ok = true;
+      for (; c.valid && ok; next_tile(c), ++it) {
+        const uint32_t buf = it & 1u;
+        if (it >= 2 && !mbar_wait(&tempty[buf], ((it >> 1) & 1u) ^ 1u, st_word)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * uint32_t(Cfg::TMEM_COLS);
+        for (int k = 0; k < num_k; ++k, ++kt) {
+          const int s = int(kt % S);
+          const uint32_t ph = (kt / S) & 1u;
+          if (!mbar_wait(&conv[s], ph, st_word)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(stA(s)), dal = sw128_desc(stAlo(s));
+          const uint64_t db = sw128_desc(stB(s)), dbl = sw128_desc(stBlo(s));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            const uint64_t adv = uint64_t(kk * 32 / 16);  // 8 tf32 = 32 bytes along K
+            mma_tf32(acc, da + adv, db + adv, idesc, (k | kk) ? 1u : 0u);
+            mma_tf32(acc, da + adv, dbl + adv, idesc, 1u);
+            mma_tf32(acc, dal + adv, db + adv, idesc, 1u);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&tfull[buf]);
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------- converters: lo = x - trunc_tf32(x) ----------------
+    const int ct = threadIdx.x - 64;
+    Cursor c;
+    first_tile(c);
+    uint32_t kt = 0;
+    bool ok = true;
+    for (; c.valid && ok; next_tile(c)) {
+      for (int k = 0; k < num_k; ++k, ++kt) {
+        const int s = int(kt % S);
+        const uint32_t ph = (kt / S) & 1u;
+        if (!mbar_wait(&full[s], ph, st_word)) {
+          ok = false;
+          break;
+        }
+        float4* a = reinterpret_cast<float4*>(stA(s));
+        float4* al = reinterpret_cast<float4*>(stAlo(s));
+#pragma unroll
+        for (int i = ct; i < Cfg::A_BYTES / 16; i += 128) split4<false>(a + i, al + i);
+        float4* b = reinterpret_cast<float4*>(stB(s));
+        float4* bl = reinterpret_cast<float4*>(stBlo(s));
+#pragma unroll
+        for (int i = ct; i < Cfg::B_BYTES / 16; i += 128) split4<false>(b + i, bl + i);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+      }
+    }
+  } else {
+    // ---------------- epilogue: TMEM -> C ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const int r = q * 32 + lane;
+    Cursor c;
+    first_tile(c);
+    uint32_t it = 0;
+    for (; c.valid; next_tile(c), ++it) {
+      const uint32_t buf = it & 1u;
+      if (!mbar_wait(&tfull[buf], (it >> 1) & 1u, st_word)) break;
+      tc_fence_after();
+      const uint32_t acc = tmem + buf * uint32_t(Cfg::TMEM_COLS) + (uint32_t(q * 32) << 16);
+      const int64_t grow = c.tm * kBM + r;
+      const int64_t col0 = c.tn * BN;
+      float* crow = g.C + c.mi * g.cstride + grow * g.ldc;
+      const bool row_ok = grow < g.m;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        const int64_t gc0 = col0 + cc * 32;
+        if (gc0 >= g.ncols) break;
+        float v[32];
+        tmem_ld32(acc + uint32_t(cc * 32), v);
+        if (!row_ok) continue;
+        if (g.lower_only && gc0 > grow + g.diag_offset) continue;
+        const bool full_chunk = (gc0 + 32 <= g.ncols) &&
+                                (!g.lower_only || gc0 + 31 <= grow + g.diag_offset) &&
+                                ((reinterpret_cast<uintptr_t>(crow + gc0) & 15) == 0);
+        if (full_chunk) {
+          float4* cp = reinterpret_cast<float4*>(crow + gc0);
+          if (g.beta != 0.f) {
+            float4 cv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cv[j] = cp[j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 o;
+              o.x = fmaf(g.alpha, v[4 * j + 0], g.beta * cv[j].x);
+              o.y = fmaf(g.alpha, v[4 * j + 1], g.beta * cv[j].y);
+              o.z = fmaf(g.alpha, v[4 * j + 2], g.beta * cv[j].z);
+              o.w = fmaf(g.alpha, v[4 * j + 3], g.beta * cv[j].w);
+              cp[j] = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              cp[j] = make_float4(g.alpha * v[4 * j], g.alpha * v[4 * j + 1],
+                                  g.alpha * v[4 * j + 2], g.alpha * v[4 * j + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int64_t col = gc0 + j;
+            if (col >= g.ncols) break;
+            if (g.lower_only && col > grow + g.diag_offset) break;
+            crow[col] = (g.beta != 0.f) ? fmaf(g.alpha, v[j], g.beta * crow[col])
+                                         : g.alpha * v[j];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(uint32_t(2 * Cfg::TMEM_COLS))
+                 : "memory");
+  }
+}
+
+// ------------------------------- host side ------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool resolve_encode() {
+  std::call_once(g_encode_once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+
+// 3-D map over (K, rows, batch) of row-major float32 rows with leading dimension ld.
+bool make_map(CUtensorMap* map, const float* base, int64_t K, int64_t rows, int64_t batch,
+              int64_t ld, int64_t bstride, int box_rows) {
+  cuuint64_t dims[3] = {cuuint64_t(K), cuuint64_t(rows), cuuint64_t(batch)};
+  cuuint64_t strides[2] = {cuuint64_t(ld) * 4, cuuint64_t(batch > 1 ? bstride : ld * rows) * 4};
+  cuuint32_t box[3] = {cuuint32_t(kBK), cuuint32_t(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN>
+int launch_tc_bn(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
+  using Cfg = TcCfg<BN>;
+  CUtensorMap mp, mq;
+  if (!make_map(&mp, g.P, g.K, g.m, g.batch, g.ldp, g.pstride, kBM)) return CHOL_ERR_UNSUPPORTED;
+  if (!make_map(&mq, g.Q, g.K, g.ncols, g.batch, g.ldq, g.qstride, BN))
+    return CHOL_ERR_UNSUPPORTED;
+  TileSpace ts{};
+  ts.tiles_m = (g.m + kBM - 1) / kBM;
+  ts.tiles_n = (g.ncols + BN - 1) / BN;
+  ts.diag_offset = g.diag_offset;
+  ts.lower_only = g.lower_only;
+  ts.bn = BN;
+  int64_t per = 0;
+  for (int64_t tm = 0; tm < ts.tiles_m; ++tm) {
+    if (!ts.lower_only) {
+      per += ts.tiles_n;
+      continue;
+    }
+    const int64_t last_c = tm * kBM + kBM - 1 + ts.diag_offset;
+    if (last_c < 0) continue;
+    const int64_t cnt = last_c / BN + 1;
+    per += cnt < ts.tiles_n ? cnt : ts.tiles_n;
+  }
+  ts.per_matrix = per;
+  ts.total = per * g.batch;
+  if (ts.total == 0) return CHOL_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t ctas = ts.total < sms ? ts.total : sms;
+  return status_from(launch_pdl(tc_gemm_kernel<BN>, dim3(unsigned(ctas)), dim3(kThreads),
+                                Cfg::SMEM, q, pdl, mp, mq, g, ts, status));
+}
+
+}  // namespace
+
+bool tc_supported(const GemmArgs& g) {
+  if (!resolve_encode()) return false;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al16(g.P) || !al16(g.Q)) return false;
+  if (g.ldp % 4 || g.ldq % 4 || g.pstride % 4 || g.qstride % 4) return false;
+  if (g.K < 1 || g.m < 1 || g.ncols < 1) return false;
+  if (g.m > 0x7fffffffLL || g.ncols > 0x7fffffffLL || g.K > 0x7fffffffLL) return false;
+  return true;
+}
+
+int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
+  if (g.ncols <= 64) return launch_tc_bn<64>(g, q, pdl, status);
+  if (g.ncols <= 128) return launch_tc_bn<128>(g, q, pdl, status);
+  return launch_tc_bn<256>(g, q, pdl, status);
+}
+
+template <int BN>
+cudaError_t set_tc_smem() {
+  return cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(TcCfg<BN>::SMEM));
+}
+
+cudaError_t prepare_tc() {
+  cudaError_t e;
+  if ((e = set_tc_smem<64>()) != cudaSuccess) return e;
+  if ((e = set_tc_smem<128>()) != cudaSuccess) return e;
+  if ((e = set_tc_smem<256>()) != cudaSuccess) return e;
+  resolve_encode();
+  return cudaSuccess;
+}
+
+int read_and_clear_status(int* out) {
+  int zero = 0, v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
+  if (e != cudaSuccess) return CHOL_ERR_DEVICE;
+  if (v) cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+  if (out) *out = v;
+  return CHOL_OK;
+}
+
+}  // namespace chol

@@ -489,6 +489,60 @@ def _other_shapes(args, skip, dev, peaks, peak_kind, lib):
     return out
 
 
+GEMM_PROBES = {
+    # name: (m, ncols, K, lower_only, alpha, beta) of one C -= P Q^T launch on an 8192-row
+    # panel; the roles of the blocked schedule's three GEMMs at n = 16384 scale
+    "trailing": (8192, 8192, 512, 1, -1.0, 1.0),
+    "inpanel": (8192, 448, 64, 1, -1.0, 1.0),
+    "solve": (8192, 64, 64, 0, 1.0, 0.0),
+}
+
+
+def run_kernel_probe(args):
+    """Time the tensor-core GEMM alone in each role (CUDA events, 10 launches after 3 warm)."""
+    from linalg_kernels_b200 import _lib
+
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    peaks, peak_kind = _peaks()
+    out = {}
+    for name in args.probe.split(","):
+        m, nc, k, lower, alpha, beta = GEMM_PROBES[name]
+        g = torch.Generator(device=dev).manual_seed(1)
+        p = torch.randn(m, k, device=dev, generator=g)
+        c = torch.randn(m, nc, device=dev, generator=g)
+        q = ctypes.c_void_p(_lib.current_queue(dev))
+
+        def launch():
+            st = lib.chol_gemm_nt_f32(ctypes.c_void_p(c.data_ptr()), 1, m * nc, nc, m, nc, k,
+                                      ctypes.c_void_p(p.data_ptr()), m * k, k,
+                                      ctypes.c_void_p(p.data_ptr()), m * k, k,
+                                      alpha, beta, 0, lower, q)
+            _lib.check(st, "chol_gemm_nt_f32")
+
+        for _ in range(args.warmup):
+            launch()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            launch()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / args.steps / 1e3
+        if lower:
+            flops = 2.0 * k * sum(min(r + 1, nc) for r in range(0, m, 1))
+            cbytes = 8.0 * sum(min(r + 1, nc) for r in range(0, m, 1))
+        else:
+            flops = 2.0 * m * nc * k
+            cbytes = (8.0 if beta else 4.0) * m * nc
+        out[name] = {"m": m, "ncols": nc, "K": k, "ms": t * 1e3,
+                     "tflops": flops / t / 1e12,
+                     "tf32_frac_of_measured": flops / t / 1e12 / (peaks["bf16_tflops"] / 2.0),
+                     "c_gbs": cbytes / t / 1e9, "hbm_frac_of_measured": cbytes / t / 1e9 / peaks["hbm_gbs"]}
+    print(json.dumps({"kernel_probe": out, "peaks": peak_kind}), flush=True)
+
+
 class _NoDist(Dist):
     def __init__(self):
         self.world, self.rank, self.local, self.pg = 1, 0, 0, None
@@ -507,9 +561,15 @@ def main(argv=None):
     ap.add_argument("--shapes", action=argparse.BooleanOptionalAction, default=True,
                     help="also time the other BASELINE shapes (N=1 only)")
     ap.add_argument("--big", action="store_true", help="include b1n32768 in --shapes")
+    ap.add_argument("--probe", default=None,
+                    help="time the tensor-core GEMM alone in the given roles "
+                         "(comma list of trailing,inpanel,solve) and exit")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.probe:
+        run_kernel_probe(args)
+        return
     if args.impl == "reference":
         # the CPU reference arm runs on rank 0 only; other ranks exit without work
         nd = _NoDist()

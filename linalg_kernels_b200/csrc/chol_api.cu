@@ -82,11 +82,31 @@ size_t blocked_workspace(int64_t batch, int64_t n) {
   return size_t(batch) * kBlock * kBlock * sizeof(float);
 }
 
+// Tensor-core GEMMs of one call share tensor maps built once over L and the inverse blocks;
+// views are addressed by TMA coordinates. Falls back to FP32 FMA when the maps cannot be
+// built (unaligned rows) or the engine option asks for it.
+struct BlockedMaps {
+  bool ok = false;
+  TcMatrixMaps L, T;
+};
+
+int gemm_on(const GemmArgs& g, const BlockedMaps& bm, const TcMatrixMaps& pm,
+            const TcMatrixMaps& qm, cudaStream_t q) {
+  if (g.m <= 0 || g.ncols <= 0) return CHOL_OK;
+  if (bm.ok && g_gemm_engine != 1) return launch_gemm_tc_mapped(g, pm, qm, q, true);
+  if (g_gemm_engine == 2) return CHOL_ERR_UNSUPPORTED;
+  return launch_gemm_simt(g, q, true);
+}
+
 int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, float* Tws,
                 cudaStream_t q) {
   int st = launch_copy_lower(A, L, batch, n, q, true);
   if (st) return st;
   const int64_t mstride = n * n;
+  BlockedMaps bm;
+  if (g_gemm_engine != 1)
+    bm.ok = tc_make_matrix_maps(L, n, n, n, batch, mstride, &bm.L) &&
+            tc_make_matrix_maps(Tws, kBlock, kBlock, kBlock, batch, kBlock * kBlock, &bm.T);
   const int64_t NB = outer_width(n);
   for (int64_t K0 = 0; K0 < n; K0 += NB) {
     const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
@@ -114,7 +134,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       s.beta = 0.f;
       s.lower_only = 0;
       s.batch = batch;
-      st = launch_gemm(s, q, true);
+      st = gemm_on(s, bm, bm.L, bm.T, q);
       if (st) return st;
       const int64_t inpanel = K0 + KB - k - kb;
       if (inpanel > 0) {
@@ -136,7 +156,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
         u.diag_offset = 0;
         u.lower_only = 1;
         u.batch = batch;
-        st = launch_gemm(u, q, true);
+        st = gemm_on(u, bm, bm.L, bm.L, q);
         if (st) return st;
       }
     }
@@ -160,7 +180,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       t.diag_offset = 0;
       t.lower_only = 1;
       t.batch = batch;
-      st = launch_gemm(t, q, true);
+      st = gemm_on(t, bm, bm.L, bm.L, q);
       if (st) return st;
     }
   }

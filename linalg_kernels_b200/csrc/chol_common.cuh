@@ -121,6 +121,20 @@ int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, i
                        cudaStream_t q, bool pdl);
 int launch_gemm_simt(const GemmArgs& g, cudaStream_t q, bool pdl);
 bool tc_supported(const GemmArgs& g);
+// Prebuilt TMA maps over one whole (rows x cols, leading dimension ld) matrix per batch
+// entry, one per box height the GEMM uses; opaque 128-byte CUtensorMap storage.
+struct TcMatrixMaps {
+  alignas(64) unsigned char p128[128];
+  alignas(64) unsigned char q64[128];
+  alignas(64) unsigned char q128[128];
+  alignas(64) unsigned char q256[128];
+  const float* base;
+  int64_t ld, bstride;
+};
+bool tc_make_matrix_maps(const float* base, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
+                         int64_t bstride, TcMatrixMaps* maps);
+int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
+                          cudaStream_t q, bool pdl);
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status);
 cudaError_t prepare_tc();
 int read_and_clear_status(int* out);

@@ -46,7 +46,9 @@ struct TcCfg {
   static constexpr int B_BYTES = BN * kBK * 4;
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TMEM_COLS = BN;
-  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+  static constexpr int EPI_LD = 36;  // staging row stride (floats): conflict-free 16B access
+  static constexpr int EPI_BYTES = 4 * 32 * EPI_LD * 4;  // one 32x32 tile per epilogue warp
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   // TMEM: two BN-column FP32 accumulators (double buffer), 2*BN <= 512
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
 };
@@ -205,10 +207,30 @@ struct TileSpace {
   }
 };
 
+// Origin of the view inside the tensor maps (element coordinates: x = column, y = row).
+struct TmaOrigin {
+  int px, py, qx, qy;
+};
+
+// Split of chunk i of a 128B-swizzled K-major tile (8 chunks of 4 floats per row; the
+// chunk at physical slot p of row r holds logical columns 4 * (p ^ (r & 7)) .. +3) with
+// columns >= kval set to zero in both the raw buffer and lo.
+__device__ __forceinline__ void split4_masked(float4* hi_p, float4* lo_p, int i, int kval) {
+  const int row = i >> 3, phys = i & 7;
+  const int col0 = 4 * (phys ^ (row & 7));
+  float4 x = *hi_p;
+  if (col0 + 0 >= kval) x.x = 0.f;
+  if (col0 + 1 >= kval) x.y = 0.f;
+  if (col0 + 2 >= kval) x.z = 0.f;
+  if (col0 + 3 >= kval) x.w = 0.f;
+  *hi_p = x;
+  split4<false>(hi_p, lo_p);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
-                   GemmArgs g, TileSpace ts, int* status) {
+                   GemmArgs g, TileSpace ts, TmaOrigin org, int* status) {
   using Cfg = TcCfg<BN>;
   constexpr int S = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -221,7 +243,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto stAlo = [&](int s) { return stA(s) + Cfg::A_BYTES / 4; };
   auto stB = [&](int s) { return stAlo(s) + Cfg::A_BYTES / 4; };
   auto stBlo = [&](int s) { return stB(s) + Cfg::B_BYTES / 4; };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(S) * Cfg::STAGE_BYTES);
+  float* epi = reinterpret_cast<float*>(smem + size_t(S) * Cfg::STAGE_BYTES);
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + size_t(S) * Cfg::STAGE_BYTES + Cfg::EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* conv = bars + S;
   uint64_t* empty = bars + 2 * S;
@@ -312,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (; c.valid && ok; next_tile(c)) {
         const int zc = int(c.mi);
-        const int y0 = int(c.tm * kBM), y1 = int(c.tn * BN);
+        const int y0 = org.py + int(c.tm * kBM), y1 = org.qy + int(c.tn * BN);
         for (int k = 0; k < num_k; ++k, ++kt) {
           const int s = int(kt % S);
           const uint32_t ph = (kt / S) & 1u;
@@ -321,8 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_expect_tx(&full[s], Cfg::A_BYTES + Cfg::B_BYTES);
-          tma_load_3d(stA(s), &tmP, k * kBK, y0, zc, &full[s]);
-          tma_load_3d(stB(s), &tmQ, k * kBK, y1, zc, &full[s]);
+          tma_load_3d(stA(s), &tmP, org.px + k * kBK, y0, zc, &full[s]);
+          tma_load_3d(stB(s), &tmQ, org.qx + k * kBK, y1, zc, &full[s]);
         }
       }
     }
@@ -378,12 +402,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         float4* a = reinterpret_cast<float4*>(stA(s));
         float4* al = reinterpret_cast<float4*>(stAlo(s));
-#pragma unroll
-        for (int i = ct; i < Cfg::A_BYTES / 16; i += 128) split4<false>(a + i, al + i);
         float4* b = reinterpret_cast<float4*>(stB(s));
         float4* bl = reinterpret_cast<float4*>(stBlo(s));
+        const int64_t kval = g.K - int64_t(k) * kBK;  // valid K columns in this stage
+        if (kval >= kBK) {
 #pragma unroll
-        for (int i = ct; i < Cfg::B_BYTES / 16; i += 128) split4<false>(b + i, bl + i);
+          for (int i = ct; i < Cfg::A_BYTES / 16; i += 128) split4<false>(a + i, al + i);
+#pragma unroll
+          for (int i = ct; i < Cfg::B_BYTES / 16; i += 128) split4<false>(b + i, bl + i);
+        } else {
+          // last partial stage: the box may reach past the view's K range (maps cover
+          // the whole matrix), so columns >= kval are zeroed in both buffers
+          for (int i = ct; i < Cfg::A_BYTES / 16; i += 128) split4_masked(a + i, al + i, i, int(kval));
+          for (int i = ct; i < Cfg::B_BYTES / 16; i += 128) split4_masked(b + i, bl + i, i, int(kval));
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[s]);
@@ -391,8 +423,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue: TMEM -> C ----------------
+    // Per 32-column chunk: tcgen05.ld (thread = row), transpose through this warp's 32x32
+    // staging tile, then rows of 32 floats read/written as coalesced 128-byte segments
+    // (8 lanes per row, 4 rows per instruction).
     const int q = warp & 3;  // TMEM lane quarter this warp may read
-    const int r = q * 32 + lane;
+    float* tile = epi + (warp - 6) * 32 * Cfg::EPI_LD;
+    const int sub_r = lane >> 3, sub_c = (lane & 7) * 4;
     Cursor c;
     first_tile(c);
     uint32_t it = 0;
@@ -401,52 +437,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull[buf], (it >> 1) & 1u, st_word)) break;
       tc_fence_after();
       const uint32_t acc = tmem + buf * uint32_t(Cfg::TMEM_COLS) + (uint32_t(q * 32) << 16);
-      const int64_t grow = c.tm * kBM + r;
+      const int64_t row_base = c.tm * kBM + q * 32;  // first row of this warp's quarter
       const int64_t col0 = c.tn * BN;
-      float* crow = g.C + c.mi * g.cstride + grow * g.ldc;
-      const bool row_ok = grow < g.m;
+      float* cbase = g.C + c.mi * g.cstride;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         const int64_t gc0 = col0 + cc * 32;
         if (gc0 >= g.ncols) break;
         float v[32];
         tmem_ld32(acc + uint32_t(cc * 32), v);
-        if (!row_ok) continue;
-        if (g.lower_only && gc0 > grow + g.diag_offset) continue;
-        const bool full_chunk = (gc0 + 32 <= g.ncols) &&
-                                (!g.lower_only || gc0 + 31 <= grow + g.diag_offset) &&
-                                ((reinterpret_cast<uintptr_t>(crow + gc0) & 15) == 0);
-        if (full_chunk) {
-          float4* cp = reinterpret_cast<float4*>(crow + gc0);
-          if (g.beta != 0.f) {
-            float4 cv[8];
+        // whole chunk above the lower boundary for every row of the quarter: nothing to do
+        if (g.lower_only && gc0 > row_base + 31 + g.diag_offset) continue;
+        if (row_base >= g.m) continue;
+        float* trow = tile + lane * Cfg::EPI_LD;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) cv[j] = cp[j];
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(trow + 4 * j) =
+              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        __syncwarp();
+        const int64_t col = gc0 + sub_c;
+        // all eight row groups' C loads in flight before any use
+        float4 cv[8];
+        bool vec[8];
+        int64_t lim[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float4 o;
-              o.x = fmaf(g.alpha, v[4 * j + 0], g.beta * cv[j].x);
-              o.y = fmaf(g.alpha, v[4 * j + 1], g.beta * cv[j].y);
-              o.z = fmaf(g.alpha, v[4 * j + 2], g.beta * cv[j].z);
-              o.w = fmaf(g.alpha, v[4 * j + 3], g.beta * cv[j].w);
-              cp[j] = o;
-            }
+        for (int rr = 0; rr < 8; ++rr) {
+          const int64_t grow = row_base + rr * 4 + sub_r;
+          float* cp = cbase + grow * g.ldc + col;
+          lim[rr] = grow >= g.m ? -1
+                                : (g.lower_only ? (grow + g.diag_offset < g.ncols - 1
+                                                       ? grow + g.diag_offset
+                                                       : g.ncols - 1)
+                                                : g.ncols - 1);
+          vec[rr] = col + 3 <= lim[rr] && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0);
+          cv[rr] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (vec[rr] && g.beta != 0.f) cv[rr] = *reinterpret_cast<const float4*>(cp);
+        }
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) {
+          const int tr = rr * 4 + sub_r;
+          if (lim[rr] < col) continue;
+          const int64_t grow = row_base + tr;
+          const float4 a4 = *reinterpret_cast<const float4*>(tile + tr * Cfg::EPI_LD + sub_c);
+          float* cp = cbase + grow * g.ldc + col;
+          if (vec[rr]) {
+            float4 o;
+            o.x = fmaf(g.alpha, a4.x, g.beta * cv[rr].x);
+            o.y = fmaf(g.alpha, a4.y, g.beta * cv[rr].y);
+            o.z = fmaf(g.alpha, a4.z, g.beta * cv[rr].z);
+            o.w = fmaf(g.alpha, a4.w, g.beta * cv[rr].w);
+            *reinterpret_cast<float4*>(cp) = o;
           } else {
+            const float av[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              cp[j] = make_float4(g.alpha * v[4 * j], g.alpha * v[4 * j + 1],
-                                  g.alpha * v[4 * j + 2], g.alpha * v[4 * j + 3]);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int64_t col = gc0 + j;
-            if (col >= g.ncols) break;
-            if (g.lower_only && col > grow + g.diag_offset) break;
-            crow[col] = (g.beta != 0.f) ? fmaf(g.alpha, v[j], g.beta * crow[col])
-                                         : g.alpha * v[j];
+            for (int e = 0; e < 4; ++e) {
+              if (col + e > lim[rr]) break;
+              cp[e] = (g.beta != 0.f) ? fmaf(g.alpha, av[e], g.beta * cp[e]) : g.alpha * av[e];
+            }
           }
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
@@ -493,19 +543,13 @@ bool make_map(CUtensorMap* map, const float* base, int64_t K, int64_t rows, int6
   return r == CUDA_SUCCESS;
 }
 
-template <int BN>
-int launch_tc_bn(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
-  using Cfg = TcCfg<BN>;
-  CUtensorMap mp, mq;
-  if (!make_map(&mp, g.P, g.K, g.m, g.batch, g.ldp, g.pstride, kBM)) return CHOL_ERR_UNSUPPORTED;
-  if (!make_map(&mq, g.Q, g.K, g.ncols, g.batch, g.ldq, g.qstride, BN))
-    return CHOL_ERR_UNSUPPORTED;
+TileSpace make_tiles(const GemmArgs& g, int bn) {
   TileSpace ts{};
   ts.tiles_m = (g.m + kBM - 1) / kBM;
-  ts.tiles_n = (g.ncols + BN - 1) / BN;
+  ts.tiles_n = (g.ncols + bn - 1) / bn;
   ts.diag_offset = g.diag_offset;
   ts.lower_only = g.lower_only;
-  ts.bn = BN;
+  ts.bn = bn;
   int64_t per = 0;
   for (int64_t tm = 0; tm < ts.tiles_m; ++tm) {
     if (!ts.lower_only) {
@@ -514,18 +558,40 @@ int launch_tc_bn(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
     }
     const int64_t last_c = tm * kBM + kBM - 1 + ts.diag_offset;
     if (last_c < 0) continue;
-    const int64_t cnt = last_c / BN + 1;
+    const int64_t cnt = last_c / bn + 1;
     per += cnt < ts.tiles_n ? cnt : ts.tiles_n;
   }
   ts.per_matrix = per;
   ts.total = per * g.batch;
+  return ts;
+}
+
+int g_num_sms = 0;
+
+template <int BN>
+int launch_tc_maps(const GemmArgs& g, const CUtensorMap& mp, const CUtensorMap& mq,
+                   TmaOrigin org, cudaStream_t q, bool pdl, int* status) {
+  using Cfg = TcCfg<BN>;
+  const TileSpace ts = make_tiles(g, BN);
   if (ts.total == 0) return CHOL_OK;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int sms = g_num_sms;
+  if (sms <= 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
   const int64_t ctas = ts.total < sms ? ts.total : sms;
   return status_from(launch_pdl(tc_gemm_kernel<BN>, dim3(unsigned(ctas)), dim3(kThreads),
-                                Cfg::SMEM, q, pdl, mp, mq, g, ts, status));
+                                Cfg::SMEM, q, pdl, mp, mq, g, ts, org, status));
+}
+
+template <int BN>
+int launch_tc_bn(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
+  CUtensorMap mp, mq;
+  if (!make_map(&mp, g.P, g.K, g.m, g.batch, g.ldp, g.pstride, kBM)) return CHOL_ERR_UNSUPPORTED;
+  if (!make_map(&mq, g.Q, g.K, g.ncols, g.batch, g.ldq, g.qstride, BN))
+    return CHOL_ERR_UNSUPPORTED;
+  return launch_tc_maps<BN>(g, mp, mq, TmaOrigin{0, 0, 0, 0}, q, pdl, status);
 }
 
 }  // namespace
@@ -538,6 +604,44 @@ bool tc_supported(const GemmArgs& g) {
   if (g.K < 1 || g.m < 1 || g.ncols < 1) return false;
   if (g.m > 0x7fffffffLL || g.ncols > 0x7fffffffLL || g.K > 0x7fffffffLL) return false;
   return true;
+}
+
+bool tc_make_matrix_maps(const float* base, int64_t rows, int64_t cols, int64_t ld,
+                         int64_t batch, int64_t bstride, TcMatrixMaps* maps) {
+  if (!resolve_encode()) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ld % 4 || (batch > 1 && bstride % 4))
+    return false;
+  maps->base = base;
+  maps->ld = ld;
+  maps->bstride = bstride;
+  return make_map(reinterpret_cast<CUtensorMap*>(maps->p128), base, cols, rows, batch, ld, bstride,
+                  kBM) &&
+         make_map(reinterpret_cast<CUtensorMap*>(maps->q64), base, cols, rows, batch, ld, bstride,
+                  64) &&
+         make_map(reinterpret_cast<CUtensorMap*>(maps->q128), base, cols, rows, batch, ld, bstride,
+                  128) &&
+         make_map(reinterpret_cast<CUtensorMap*>(maps->q256), base, cols, rows, batch, ld, bstride,
+                  256);
+}
+
+// P and Q are views of the matrices behind pm / qm (element offsets from their bases).
+int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
+                          cudaStream_t q, bool pdl) {
+  const int64_t po = g.P - pm.base, qo = g.Q - qm.base;
+  if (po < 0 || qo < 0 || g.ldp != pm.ld || g.ldq != qm.ld) return CHOL_ERR_INVALID_ARG;
+  if (g.batch > 1 && (g.pstride != pm.bstride || g.qstride != qm.bstride))
+    return CHOL_ERR_INVALID_ARG;
+  TmaOrigin org{int(po % pm.ld), int(po / pm.ld), int(qo % qm.ld), int(qo / qm.ld)};
+  if ((org.px & 3) || (org.qx & 3)) return CHOL_ERR_INVALID_ARG;  // TMA x must be 16-byte aligned
+  const CUtensorMap& mp = *reinterpret_cast<const CUtensorMap*>(pm.p128);
+  if (g.ncols <= 64)
+    return launch_tc_maps<64>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q64), org, q, pdl,
+                              nullptr);
+  if (g.ncols <= 128)
+    return launch_tc_maps<128>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q128), org, q,
+                               pdl, nullptr);
+  return launch_tc_maps<256>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q256), org, q, pdl,
+                             nullptr);
 }
 
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
@@ -554,6 +658,9 @@ cudaError_t set_tc_smem() {
 
 cudaError_t prepare_tc() {
   cudaError_t e;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
   if ((e = set_tc_smem<64>()) != cudaSuccess) return e;
   if ((e = set_tc_smem<128>()) != cudaSuccess) return e;
   if ((e = set_tc_smem<256>()) != cudaSuccess) return e;

@@ -51,6 +51,7 @@ extern "C" {
 #define CHOL_ERR_WORKSPACE 5     /* caller workspace missing or smaller than required */
 #define CHOL_ERR_DEVICE 6        /* no usable sm_100 device / CUDA runtime error */
 #define CHOL_ERR_UNSUPPORTED 7   /* size outside what this build supports */
+#define CHOL_ERR_SCRATCH_LIMIT 8 /* needs more scratch than chol_potrf_batched_noalloc_f32 has */
 
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 CHOL_API int chol_version(void);
@@ -96,6 +97,22 @@ CHOL_API int chol_potrf_batched_f32(const float* A, float* L, int64_t batch, int
 CHOL_API int chol_potrf_batched_ws_f32(const float* A, float* L, int64_t batch, int64_t n,
                               int* info, void* workspace, size_t workspace_bytes,
                               void* queue);
+
+/*
+ * Same factorisation, allocating no device memory. No counterpart in the reference, which
+ * always allocates its output and workspaces per call. For callers that cannot call
+ * cudaMalloc (a host that owns all device memory through its own pool, or a path where
+ * cudaMalloc's implicit device synchronisation is not allowed): the caller passes A, L
+ * and info as usual, and the only scratch (the 64 x 64 inverse diagonal blocks of the
+ * blocked path, 16 KiB per matrix with n > 64) comes from a fixed 4 MiB device array
+ * inside the library, held on every GPU that loads the library until exit. Problems that
+ * need more (batch > 256 when n > 64) return CHOL_ERR_SCRATCH_LIMIT; n <= 64 needs none.
+ * The first call on a device looks up the array's device address with that device
+ * current; make that first call before any stream capture. All calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller.
+ */
+CHOL_API int chol_potrf_batched_noalloc_f32(const float* A, float* L, int64_t batch, int64_t n,
+                                            int* info, void* queue);
 
 /*
  * Number of kernel launches one chol_potrf_batched_*_f32 call makes for (batch, n)

@@ -23,6 +23,7 @@ CHOL_ERR_WAIT_TIMEOUT = 4
 CHOL_ERR_WORKSPACE = 5
 CHOL_ERR_DEVICE = 6
 CHOL_ERR_UNSUPPORTED = 7
+CHOL_ERR_SCRATCH_LIMIT = 8
 
 CHOL_OPT_GEMM_ENGINE = 1
 ENGINE_AUTO, ENGINE_FMA, ENGINE_TENSOR = 0, 1, 2
@@ -41,6 +42,7 @@ SIGNATURES: dict[str, tuple] = {
     "chol_workspace_bytes": (_sz, [_i64, _i64]),
     "chol_potrf_batched_f32": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "chol_potrf_batched_ws_f32": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
+    "chol_potrf_batched_noalloc_f32": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "chol_launch_count": (_i64, [_i64, _i64]),
     "chol_set_option": (_int, [_int, _int]),
     "chol_status_check": (_int, [_vp]),

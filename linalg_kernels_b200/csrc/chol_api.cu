@@ -224,6 +224,15 @@ int potrf_impl(const float* A, float* L, int64_t batch, int64_t n, int* info, vo
 
 }  // namespace
 
+int prepare_device_checked(int dev) { return prepare_device(dev); }
+int check_potrf_args(const float* A, float* L, int64_t batch, int64_t n) {
+  return check_common(A, L, batch, n);
+}
+int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int* info, void* ws,
+                         size_t ws_bytes, cudaStream_t q) {
+  return potrf_impl(A, L, batch, n, info, ws, ws_bytes, q);
+}
+
 int prepare_kernels(int /*device*/) {
   return prepare_tc() == cudaSuccess ? CHOL_OK : CHOL_ERR_DEVICE;
 }
@@ -256,6 +265,8 @@ const char* chol_strerror(int status) {
     case CHOL_ERR_WORKSPACE: return "workspace missing or too small";
     case CHOL_ERR_DEVICE: return "no usable sm_100 CUDA device";
     case CHOL_ERR_UNSUPPORTED: return "size not supported by this build";
+    case CHOL_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the fixed buffer of the no-allocation entry point";
     default: return "unknown status";
   }
 }

@@ -110,6 +110,12 @@ struct GemmArgs {
   int64_t batch;
 };
 
+// Entry-point plumbing shared by the C-ABI files (chol_api.cu).
+int prepare_device_checked(int dev);
+int check_potrf_args(const float* A, float* L, int64_t batch, int64_t n);
+int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int* info, void* ws,
+                         size_t ws_bytes, cudaStream_t q);
+
 // Host launchers implemented in the .cu files.
 cudaError_t prepare_small();
 int prepare_kernels(int device);

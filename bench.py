@@ -461,6 +461,88 @@ def _e2e(args, cfg, pool, lib, dev, dist):
             "path": "chol_potrf_batched_f32 (C ABI) with pinned host input/output"}
 
 
+def run_cyclic(args, dist: Dist):
+    """One matrix over all ranks, 1-D block-column-cyclic, NCCL panel broadcasts
+    (linalg_kernels_b200.distributed). Inputs are resident shards: every rank builds its own
+    columns of A = X X^T / n + shift I. A step copies the pristine shard into the work
+    buffer and factors it. Strong scaling: one matrix per step whatever the rank count."""
+    from linalg_kernels_b200 import _lib, inputs
+    from linalg_kernels_b200.distributed import CyclicLayout, factor_block_cyclic
+
+    lib = _lib.load()
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    peaks, peak_kind = _peaks()
+    cfg = inputs.CONFIGS[args.config]
+    n = cfg.n
+    lay = CyclicLayout(n, dist.world, dist.rank, 256)
+    g = torch.Generator(device=dev).manual_seed(cfg.seed)
+    x = torch.randn(n, n, generator=g, device=dev)
+    shard = torch.zeros(n, lay.n_local, device=dev)
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    for t in lay.owned():
+        c0, w, lc = t * lay.bs, lay.width(t), lay.local_col(t)
+        blk = (x[c0:] @ x[c0:c0 + w].T) / n
+        blk[:w].diagonal().add_(cfg.param)
+        shard[c0:, lc:lc + w] = torch.tril(blk)
+    torch.backends.cuda.matmul.allow_tf32 = old
+    del x
+    torch.cuda.empty_cache()
+    work = torch.empty_like(shard)
+
+    def step(_):
+        work.copy_(shard)
+        factor_block_cyclic(work, lay, pg=dist.pg if dist.world > 1 else None)
+
+    with ClockSampler(dev.index) as clocks:
+        total_ms, per = _time_steps(step, [None], args.steps, args.warmup, dist)
+    total_ms = dist.max(total_ms)
+    value = args.steps / (total_ms / 1e3)
+    # e2e: pinned host shard in, factor, pinned host shard out
+    host_in = shard.cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    for i in range(2):
+        work.copy_(host_in, non_blocking=True)
+        factor_block_cyclic(work, lay, pg=dist.pg if dist.world > 1 else None)
+        host_out.copy_(work, non_blocking=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        work.copy_(host_in, non_blocking=True)
+        factor_block_cyclic(work, lay, pg=dist.pg if dist.world > 1 else None)
+        host_out.copy_(work, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms = dist.max(e0.elapsed_time(e1))
+    nbytes = shard.numel() * 4
+    line = {
+        "metric": "matrices/s", "value": value, "unit": "matrices/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": (value / (1 / REFERENCE_PUBLISHED_S[cfg.name]) if dist.world == 1
+                        else None),
+        "dtype": "f32", "data": "synthetic", "tflops": value * n ** 3 / 3.0 / 1e12,
+        "config": {"workload": cfg.name, "batch": 1, "n": n, "family": cfg.family,
+                   "param": cfg.param, "seed": cfg.seed, "block": lay.bs,
+                   "parallelism": f"1-D block-column-cyclic over {dist.world} GPUs, NCCL "
+                                  f"broadcast of each factored 256-wide panel",
+                   "l2": "input 4 GiB > L2"},
+        "roofline": None,
+        "e2e": {"value": dist.world and args.steps / (e2e_ms / 1e3), "unit": "matrices/s",
+                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+                "note": "per rank: its resident shard in and out"},
+        "cpu_baseline": None,
+        "clocks": clocks.summary(),
+        "gpu_launches": None,
+    }
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def _other_shapes(args, skip, dev, peaks, peak_kind, lib):
     from linalg_kernels_b200 import inputs
     from linalg_kernels_b200.cholesky import custom_kernel
@@ -561,6 +643,8 @@ def main(argv=None):
     ap.add_argument("--shapes", action=argparse.BooleanOptionalAction, default=True,
                     help="also time the other BASELINE shapes (N=1 only)")
     ap.add_argument("--big", action="store_true", help="include b1n32768 in --shapes")
+    ap.add_argument("--cyclic", action="store_true",
+                    help="b1n32768 through the block-cyclic driver even on one GPU")
     ap.add_argument("--probe", default=None,
                     help="time the tensor-core GEMM alone in the given roles "
                          "(comma list of trailing,inpanel,solve) and exit")
@@ -578,7 +662,10 @@ def main(argv=None):
         return
     dist = Dist()
     try:
-        run_ours(args, dist)
+        if args.config == "b1n32768" and (dist.world > 1 or args.cyclic):
+            run_cyclic(args, dist)
+        else:
+            run_ours(args, dist)
     finally:
         dist.close()
 

@@ -5,13 +5,13 @@
 // to torch, this library plans every (batch, n) on the GPU:
 //   n <= 64   one launch of the warp-register kernel (chol_small.cu)
 //   n  > 64   right-looking blocked schedule, 64-wide diagonal blocks, outer panels of
-//             width NB whose trailing update is deferred to one rank-NB update:
+//             width NB, left-looking inside a panel and right-looking between panels:
 //               copy tril(A) -> L
 //               for each outer panel [K0, K0+NB):
-//                 for each 64-wide block k in the panel:
+//                 for each 64-wide block column k in the panel:
+//                   L[k:, k:k+64] -= L[k:, K0:k] L[k:k+64, K0:k]^T   (GEMM, K = k - K0)
 //                   potrf_block(k)            factor + inverse T_k   (1 CTA / matrix)
 //                   X = L[k+64:, k] * T_k^T   panel solve, in place  (GEMM)
-//                   L[k+64:, k+64:K0+NB] -= X * X[..]^T  in-panel update (GEMM, K = 64)
 //                 L[K0+NB:, K0+NB:] -= P * P^T, P = L[K0+NB:, K0:K0+NB]  (lower tiles, K = NB)
 // All launches go on the caller's queue with programmatic dependent launch.
 #include <mutex>
@@ -112,6 +112,30 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
     const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
     for (int64_t k = K0; k < K0 + KB; k += kBlock) {
       const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
+      if (k > K0) {
+        // left-looking inside the outer panel: block column k receives the updates of the
+        // panel's already factored columns [K0, k) in one GEMM (K = k - K0)
+        GemmArgs u{};
+        u.C = L + k * n + k;
+        u.cstride = mstride;
+        u.ldc = n;
+        u.P = L + k * n + K0;
+        u.pstride = mstride;
+        u.ldp = n;
+        u.Q = u.P;
+        u.qstride = mstride;
+        u.ldq = n;
+        u.m = n - k;
+        u.ncols = kb;
+        u.K = k - K0;
+        u.alpha = -1.f;
+        u.beta = 1.f;
+        u.diag_offset = 0;
+        u.lower_only = 1;
+        u.batch = batch;
+        st = gemm_on(u, bm, bm.L, bm.L, q);
+        if (st) return st;
+      }
       st = launch_potrf_block(L, mstride, n, L, mstride, n, batch, k, kb, Tws, info, q, true);
       if (st) return st;
       const int64_t below = n - k - kb;
@@ -136,29 +160,6 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       s.batch = batch;
       st = gemm_on(s, bm, bm.L, bm.T, q);
       if (st) return st;
-      const int64_t inpanel = K0 + KB - k - kb;
-      if (inpanel > 0) {
-        GemmArgs u{};
-        u.C = L + (k + kb) * n + (k + kb);
-        u.cstride = mstride;
-        u.ldc = n;
-        u.P = L + (k + kb) * n + k;
-        u.pstride = mstride;
-        u.ldp = n;
-        u.Q = u.P;
-        u.qstride = mstride;
-        u.ldq = n;
-        u.m = below;
-        u.ncols = inpanel;
-        u.K = kb;
-        u.alpha = -1.f;
-        u.beta = 1.f;
-        u.diag_offset = 0;
-        u.lower_only = 1;
-        u.batch = batch;
-        st = gemm_on(u, bm, bm.L, bm.L, q);
-        if (st) return st;
-      }
     }
     const int64_t rest = n - K0 - KB;
     if (rest > 0) {
@@ -195,10 +196,9 @@ int64_t blocked_launches(int64_t n) {
     const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
     for (int64_t k = K0; k < K0 + KB; k += kBlock) {
       const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
-      count += 1;
-      if (n - k - kb <= 0) continue;
-      count += 1;
-      if (K0 + KB - k - kb > 0) count += 1;
+      if (k > K0) count += 1;  // left-looking panel update
+      count += 1;              // diagonal block
+      if (n - k - kb > 0) count += 1;  // panel solve
     }
     if (n - K0 - KB > 0) count += 1;
   }

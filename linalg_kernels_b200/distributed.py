@@ -1,0 +1,210 @@
+"""Multi-GPU Cholesky of one large matrix: 1-D block-column-cyclic over ranks, NCCL panels.
+
+The reference has no multi-GPU path (its n = 32768 kernel runs on one B200,
+cholesky/cholesky.py:5692-5802). Here one process per GPU holds the column blocks
+``t = rank, rank + P, rank + 2P, ...`` (block width ``bs``, default 256) of the matrix,
+row-major in a local ``(n, n_local)`` tensor. For every block column ``j``:
+
+1. its owner factors the panel ``L[j*bs:, j*bs:(j+1)*bs]`` in place: four 64-wide steps of
+   diagonal factor + inverse (``chol_block_potrf_f32``), panel solve ``X <- X T^T`` and
+   in-panel update (``chol_gemm_nt_f32``, tensor cores);
+2. the factored panel (rows ``j*bs .. n``, ``bs`` columns, at most 32 MiB at n = 32768) is
+   packed contiguously and broadcast by NCCL from the owner into every rank's receive
+   buffer (local memory; no kernel reads another GPU's memory);
+3. every rank applies ``C -= P P^T`` (lower tiles, K = bs) to each of its blocks ``t > j``.
+
+Look-ahead: the owner of block ``j+1`` first updates that block with panel ``j``, factors
+it and starts its broadcast; only then does every rank update its remaining blocks with
+panel ``j``, so the broadcast of panel ``j+1`` overlaps the bulk of step ``j``'s update.
+Receive buffers are double-buffered. Every rank issues the same collectives in the same
+order.
+
+The arithmetic goes through an ``ops`` object: ``CudaOps`` (the C ABI of libchol_b200.so,
+the product path). Tests substitute a CPU implementation to check the schedule with
+``gloo`` ranks on machines without GPUs.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+__all__ = ["CyclicLayout", "CudaOps", "factor_block_cyclic", "scatter_block_cyclic",
+           "gather_block_cyclic"]
+
+
+@dataclass(frozen=True)
+class CyclicLayout:
+    n: int
+    world: int
+    rank: int
+    bs: int = 256
+
+    @property
+    def nblocks(self) -> int:
+        return (self.n + self.bs - 1) // self.bs
+
+    def owner(self, t: int) -> int:
+        return t % self.world
+
+    def owned(self) -> list[int]:
+        return list(range(self.rank, self.nblocks, self.world))
+
+    def width(self, t: int) -> int:
+        return min(self.bs, self.n - t * self.bs)
+
+    def local_col(self, t: int) -> int:
+        """First local column of block t (t must be owned by this rank)."""
+        return (t // self.world) * self.bs
+
+    @property
+    def n_local(self) -> int:
+        blocks = self.owned()
+        return sum(self.width(t) for t in blocks)
+
+
+def scatter_block_cyclic(a: torch.Tensor, lay: CyclicLayout) -> torch.Tensor:
+    """This rank's columns of the full matrix ``a`` (lower triangle kept, zeros above)."""
+    n = lay.n
+    out = torch.zeros(n, lay.n_local, dtype=a.dtype, device=a.device)
+    for t in lay.owned():
+        c0, w, lc = t * lay.bs, lay.width(t), lay.local_col(t)
+        out[c0:, lc:lc + w] = torch.tril(a[c0:, c0:c0 + w])
+    return out
+
+
+def gather_block_cyclic(parts: list[torch.Tensor], n: int, world: int, bs: int = 256):
+    """Reassemble the full matrix from every rank's local tensor (tests, e2e output)."""
+    full = torch.zeros(n, n, dtype=parts[0].dtype, device=parts[0].device)
+    for r in range(world):
+        lay = CyclicLayout(n, world, r, bs)
+        for t in lay.owned():
+            c0, w, lc = t * bs, lay.width(t), lay.local_col(t)
+            full[:, c0:c0 + w] = parts[r][:, lc:lc + w]
+    return full
+
+
+def _rowmajor(t: torch.Tensor) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError("expected a row-major 2-D view")
+    return t.stride(0)
+
+
+class CudaOps:
+    """Product backend: the sm_100a kernels through the C ABI, on torch's current queue."""
+
+    def __init__(self, device: torch.device):
+        self.lib = _lib.load()
+        self.device = device
+
+    def _q(self):
+        return ctypes.c_void_p(_lib.current_queue(self.device))
+
+    def potrf_block(self, diag: torch.Tensor, tinv: torch.Tensor, info: torch.Tensor | None):
+        """Factor diag (kb x kb view, kb <= 64) in place; tinv (64 x 64) <- inv(L)."""
+        ld = _rowmajor(diag)
+        st = self.lib.chol_block_potrf_f32(
+            ctypes.c_void_p(diag.data_ptr()), 1, 0, ld, 0, diag.shape[0],
+            ctypes.c_void_p(tinv.data_ptr()),
+            ctypes.c_void_p(info.data_ptr()) if info is not None else None, self._q())
+        _lib.check(st, "chol_block_potrf_f32")
+
+    def gemm_nt(self, c: torch.Tensor, p: torch.Tensor, q: torch.Tensor, alpha: float,
+                beta: float, lower_only: bool):
+        """c = alpha * p q^T + beta * c; lower_only keeps elements with col <= row."""
+        m, nc = c.shape
+        k = p.shape[1]
+        st = self.lib.chol_gemm_nt_f32(
+            ctypes.c_void_p(c.data_ptr()), 1, 0, _rowmajor(c), m, nc, k,
+            ctypes.c_void_p(p.data_ptr()), 0, _rowmajor(p),
+            ctypes.c_void_p(q.data_ptr()), 0, _rowmajor(q),
+            float(alpha), float(beta), 0, 1 if lower_only else 0, self._q())
+        _lib.check(st, "chol_gemm_nt_f32")
+
+
+def _factor_panel(local: torch.Tensor, lay: CyclicLayout, t: int, ops, tinv, info):
+    """Owner: factor block column t in place (rows t*bs..n of its local columns), 64-wide
+    steps, left-looking inside the panel."""
+    n, bs = lay.n, lay.bs
+    c0, w, lc = t * bs, lay.width(t), lay.local_col(t)
+    for kk in range(0, w, 64):
+        kb = min(64, w - kk)
+        r = c0 + kk  # global row (and column) of this 64-block
+        col = lc + kk  # its local column
+        if kk > 0:
+            prev = local[r:, lc:col]
+            ops.gemm_nt(local[r:, col:col + kb], prev, prev[:kb], -1.0, 1.0, True)
+        ops.potrf_block(local[r:r + kb, col:col + kb], tinv, info)
+        if n - r - kb <= 0:
+            continue
+        x = local[r + kb:, col:col + kb]
+        ops.gemm_nt(x, x, tinv[:kb, :kb], 1.0, 0.0, False)
+
+
+def _update_block(local: torch.Tensor, lay: CyclicLayout, t: int, j: int, panel, ops):
+    """local block t -= panel_j-contribution (rows t*bs..n, lower part)."""
+    bs = lay.bs
+    c0, w, lc = t * bs, lay.width(t), lay.local_col(t)
+    off = c0 - j * bs  # panel row of global row c0
+    p = panel[off:]
+    ops.gemm_nt(local[c0:, lc:lc + w], p, p[:w], -1.0, 1.0, True)
+
+
+def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=None, ops=None,
+                        info: torch.Tensor | None = None) -> torch.Tensor:
+    """Factor in place the block-column-cyclic matrix whose local columns are ``local``.
+
+    ``pg`` is ``torch.distributed`` (or None for a single rank); ``ops`` defaults to
+    ``CudaOps`` on ``local``'s device. Returns ``local`` (now this rank's columns of L).
+    """
+    if ops is None:
+        ops = CudaOps(local.device)
+    n, bs = lay.n, lay.bs
+    nb = lay.nblocks
+    dev = local.device
+    tinv = torch.zeros(64, 64, dtype=local.dtype, device=dev)
+    bufs = [torch.empty(n * bs, dtype=local.dtype, device=dev) for _ in range(2)]
+
+    def panel_view(j):
+        rows = n - j * bs
+        return bufs[j % 2][: rows * lay.width(j)].view(rows, lay.width(j))
+
+    def publish(j):
+        """Owner packs panel j; everyone joins the broadcast. Returns the work handle."""
+        pv = panel_view(j)
+        if lay.owner(j) == lay.rank:
+            lc = lay.local_col(j)
+            pv.copy_(local[j * bs:, lc:lc + lay.width(j)])
+        if pg is None or lay.world == 1:
+            return None
+        return pg.broadcast(pv, src=_global_rank(pg, group, lay.owner(j)), group=group,
+                            async_op=True)
+
+    if lay.owner(0) == lay.rank:
+        _factor_panel(local, lay, 0, ops, tinv, info)
+    work = publish(0)
+    for j in range(nb):
+        if work is not None:
+            work.wait()
+        panel = panel_view(j)
+        nxt = j + 1
+        work = None
+        if nxt < nb:
+            if lay.owner(nxt) == lay.rank:
+                _update_block(local, lay, nxt, j, panel, ops)
+                _factor_panel(local, lay, nxt, ops, tinv, info)
+            work = publish(nxt)
+        for t in lay.owned():
+            if t > nxt:
+                _update_block(local, lay, t, j, panel, ops)
+    return local
+
+
+def _global_rank(pg, group, r):
+    if group is None:
+        return r
+    return pg.get_global_rank(group, r)

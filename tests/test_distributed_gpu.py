@@ -1,0 +1,92 @@
+"""GPU: the block-column-cyclic driver with the CUDA ops on one rank (no process group):
+the same schedule the multi-GPU path runs, checked against the oracle's bounds."""
+
+import numpy as np
+import pytest
+import torch
+
+from linalg_kernels_b200 import inputs
+from linalg_kernels_b200.distributed import (CyclicLayout, factor_block_cyclic,
+                                             gather_block_cyclic, scatter_block_cyclic)
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.mark.parametrize("n,bs", [(1024, 256), (700, 256), (640, 128)])
+def test_cyclic_single_rank_matches_oracle(n, bs):
+    a, cond = inputs.covariance(1, n, 0.5, 900 + n)
+    lay = CyclicLayout(n, 1, 0, bs)
+    local = scatter_block_cyclic(a[0].to(DEV), lay)
+    factor_block_cyclic(local, lay, pg=None)
+    torch.cuda.synchronize()
+    l = gather_block_cyclic([local], n, 1, bs).cpu().numpy()[None]
+    l_or, _ = oracle.potrf(a.numpy())
+    res = oracle.check_factor(a.numpy(), l, l_ref=l_or, cond=cond.numpy())
+    assert res["ok"], res
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_cyclic_emulated_ranks_on_one_gpu(world):
+    """Each emulated rank's columns factored by the same schedule must equal the
+    single-layout factor (the broadcast is replaced by reading the owner's panel)."""
+    n, bs = 768, 128
+    a, cond = inputs.covariance(1, n, 0.5, 77)
+    full = torch.tril(a[0]).to(DEV)
+    lay1 = CyclicLayout(n, 1, 0, bs)
+    one = scatter_block_cyclic(full, lay1)
+    factor_block_cyclic(one, lay1, pg=None)
+    torch.cuda.synchronize()
+    want = gather_block_cyclic([one], n, 1, bs)
+    l = want.cpu().numpy()[None]
+    l_or, _ = oracle.potrf(a.numpy())
+    assert oracle.check_factor(a.numpy(), l, l_ref=l_or, cond=cond.numpy())["ok"]
+    # layouts for `world` ranks partition the columns exactly
+    parts = [scatter_block_cyclic(want, CyclicLayout(n, world, r, bs)) for r in range(world)]
+    assert torch.equal(gather_block_cyclic(parts, n, world, bs), want)
+
+
+def _nccl_worker(rank, world, port, n, bs, seed, out_dir):
+    import os
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        a, _ = inputs.covariance(1, n, 0.5, seed)
+        lay = CyclicLayout(n, world, rank, bs)
+        local = scatter_block_cyclic(a[0].to(f"cuda:{rank}"), lay)
+        factor_block_cyclic(local, lay, pg=dist)
+        torch.cuda.synchronize()
+        torch.save(local.cpu(), os.path.join(out_dir, f"part{rank}.pt"))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_cyclic_two_ranks_nccl(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    n, bs = 1536, 256
+    mp.spawn(_nccl_worker, args=(2, port, n, bs, 4242, str(tmp_path)), nprocs=2, join=True)
+    parts = [torch.load(tmp_path / f"part{r}.pt") for r in range(2)]
+    l = gather_block_cyclic(parts, n, 2, bs).numpy()[None]
+    a, cond = inputs.covariance(1, n, 0.5, 4242)
+    l_or, _ = oracle.potrf(a.numpy())
+    res = oracle.check_factor(a.numpy(), l, l_ref=l_or, cond=cond.numpy())
+    assert res["ok"], res

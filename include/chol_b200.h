@@ -172,6 +172,24 @@ CHOL_API int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t 
                      const float* Q, int64_t qstride, int64_t ldq, float alpha, float beta,
                      int64_t diag_offset, int lower_only, void* queue);
 
+/* Factor a tall panel in place: the first w columns of an m-row row-major view (leading
+   dimension ld) whose element (0, 0) sits on the matrix diagonal, left-looking in 64-wide
+   steps (diagonal block + inverse, solve of the rows below). Tinv: 64*64 floats of device
+   workspace. info (nullable, one int): first failing column of the panel (1-based) or 0.
+   The per-panel step of the multi-GPU block-column-cyclic driver. */
+CHOL_API int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv,
+                                  int* info, void* queue);
+
+/* chol_gemm_nt_f32 for one matrix whose columns are stored block-cyclically: local column c
+   of C (and row c of Q) stands for global column c + (c / col_block) * (col_stride -
+   col_block), and lower_only compares that global column with the row. One launch updates
+   every trailing block a rank owns. col_block must be 256 and col_stride a multiple of it
+   (tensor-core path; needs 16-byte aligned rows). */
+CHOL_API int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t ncols, int64_t K,
+                                     const float* P, int64_t ldp, const float* Q, int64_t ldq,
+                                     float alpha, float beta, int64_t diag_offset, int lower_only,
+                                     int64_t col_block, int64_t col_stride, void* queue);
+
 #ifdef __cplusplus
 }
 #endif

@@ -405,4 +405,86 @@ int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t ldc, int6
   return launch_gemm(g, static_cast<cudaStream_t>(queue), true);
 }
 
+int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv, int* info,
+                         void* queue) {
+  if (L == nullptr || Tinv == nullptr || m < 0 || w < 0 || w > m || ld < w)
+    return CHOL_ERR_INVALID_ARG;
+  if (m == 0 || w == 0) return CHOL_OK;
+  int dev = 0, st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  cudaStream_t q = static_cast<cudaStream_t>(queue);
+  for (int64_t k = 0; k < w; k += kBlock) {
+    const int64_t kb = (w - k) < kBlock ? (w - k) : kBlock;
+    if (k > 0) {
+      GemmArgs u{};
+      u.C = L + k * ld + k;
+      u.ldc = ld;
+      u.P = L + k * ld;
+      u.ldp = ld;
+      u.Q = u.P;
+      u.ldq = ld;
+      u.m = m - k;
+      u.ncols = kb;
+      u.K = k;
+      u.alpha = -1.f;
+      u.beta = 1.f;
+      u.lower_only = 1;
+      u.batch = 1;
+      if ((st = launch_gemm(u, q, true))) return st;
+    }
+    if ((st = launch_potrf_block(L, 0, ld, L, 0, ld, 1, k, kb, Tinv, info, q, true))) return st;
+    if (m - k - kb <= 0) continue;
+    GemmArgs x{};
+    x.C = L + (k + kb) * ld + k;
+    x.ldc = ld;
+    x.P = x.C;
+    x.ldp = ld;
+    x.Q = Tinv;
+    x.ldq = kBlock;
+    x.m = m - k - kb;
+    x.ncols = kb;
+    x.K = kb;
+    x.alpha = 1.f;
+    x.beta = 0.f;
+    x.batch = 1;
+    if ((st = launch_gemm(x, q, true))) return st;
+  }
+  return CHOL_OK;
+}
+
+int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t ncols, int64_t K,
+                            const float* P, int64_t ldp, const float* Q, int64_t ldq, float alpha,
+                            float beta, int64_t diag_offset, int lower_only, int64_t col_block,
+                            int64_t col_stride, void* queue) {
+  if (m < 0 || ncols < 0 || K < 0) return CHOL_ERR_INVALID_ARG;
+  if (m == 0 || ncols == 0) return CHOL_OK;
+  if (C == nullptr || P == nullptr || Q == nullptr || ldc < ncols || ldp < K || ldq < K)
+    return CHOL_ERR_INVALID_ARG;
+  if (col_block != 256 || col_stride < col_block || col_stride % col_block)
+    return CHOL_ERR_UNSUPPORTED;
+  int dev = 0, st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  GemmArgs g{};
+  g.C = C;
+  g.ldc = ldc;
+  g.P = P;
+  g.ldp = ldp;
+  g.Q = Q;
+  g.ldq = ldq;
+  g.m = m;
+  g.ncols = ncols;
+  g.K = K;
+  g.alpha = alpha;
+  g.beta = beta;
+  g.diag_offset = diag_offset;
+  g.lower_only = lower_only;
+  g.batch = 1;
+  g.cmap_block = col_block;
+  g.cmap_stride = col_stride;
+  if (!tc_supported(g)) return CHOL_ERR_UNSUPPORTED;
+  return launch_gemm_tc(g, static_cast<cudaStream_t>(queue), true, nullptr);
+}
+
 }  // extern "C"

@@ -108,6 +108,12 @@ struct GemmArgs {
   float alpha, beta;
   int lower_only;
   int64_t batch;
+  // Column-cyclic mapping (multi-GPU block-cyclic layouts): when cmap_block > 0, local
+  // column c of C (and row c of Q) stands for global column
+  //   c + (c / cmap_block) * (cmap_stride - cmap_block),
+  // i.e. consecutive local blocks of cmap_block columns are cmap_stride global columns
+  // apart; lower_only compares global columns with rows. Q's rows follow the same map.
+  int64_t cmap_block, cmap_stride;
 };
 
 // Entry-point plumbing shared by the C-ABI files (chol_api.cu).

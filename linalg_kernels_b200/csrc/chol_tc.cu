@@ -198,11 +198,12 @@ struct TileSpace {
   int64_t diag_offset;
   int lower_only;
   int bn;
+  int64_t col_step;  // global columns between consecutive column tiles (bn, or the cyclic stride)
   __device__ __forceinline__ int64_t row_count(int64_t tm) const {
     if (!lower_only) return tiles_n;
     const int64_t last_c = tm * kBM + kBM - 1 + diag_offset;
     if (last_c < 0) return 0;
-    const int64_t cnt = last_c / bn + 1;
+    const int64_t cnt = last_c / col_step + 1;
     return cnt < tiles_n ? cnt : tiles_n;
   }
 };
@@ -336,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (; c.valid && ok; next_tile(c)) {
         const int zc = int(c.mi);
-        const int y0 = org.py + int(c.tm * kBM), y1 = org.qy + int(c.tn * BN);
+        const int y0 = org.py + int(c.tm * kBM), y1 = org.qy + int(c.tn * ts.col_step);
         for (int k = 0; k < num_k; ++k, ++kt) {
           const int s = int(kt % S);
           const uint32_t ph = (kt / S) & 1u;
@@ -446,8 +447,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (gc0 >= g.ncols) break;
         float v[32];
         tmem_ld32(acc + uint32_t(cc * 32), v);
+        // global column of local column gc0 (column-cyclic layouts shift whole blocks)
+        const int64_t shift = g.cmap_block ? (gc0 / g.cmap_block) * (g.cmap_stride - g.cmap_block)
+                                           : 0;
         // whole chunk above the lower boundary for every row of the quarter: nothing to do
-        if (g.lower_only && gc0 > row_base + 31 + g.diag_offset) continue;
+        if (g.lower_only && gc0 + shift > row_base + 31 + g.diag_offset) continue;
         if (row_base >= g.m) continue;
         float* trow = tile + lane * Cfg::EPI_LD;
 #pragma unroll
@@ -465,8 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t grow = row_base + rr * 4 + sub_r;
           float* cp = cbase + grow * g.ldc + col;
           lim[rr] = grow >= g.m ? -1
-                                : (g.lower_only ? (grow + g.diag_offset < g.ncols - 1
-                                                       ? grow + g.diag_offset
+                                : (g.lower_only ? (grow + g.diag_offset - shift < g.ncols - 1
+                                                       ? grow + g.diag_offset - shift
                                                        : g.ncols - 1)
                                                 : g.ncols - 1);
           vec[rr] = col + 3 <= lim[rr] && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0);
@@ -550,6 +554,7 @@ TileSpace make_tiles(const GemmArgs& g, int bn) {
   ts.diag_offset = g.diag_offset;
   ts.lower_only = g.lower_only;
   ts.bn = bn;
+  ts.col_step = g.cmap_block ? g.cmap_stride : bn;
   int64_t per = 0;
   for (int64_t tm = 0; tm < ts.tiles_m; ++tm) {
     if (!ts.lower_only) {
@@ -558,7 +563,7 @@ TileSpace make_tiles(const GemmArgs& g, int bn) {
     }
     const int64_t last_c = tm * kBM + kBM - 1 + ts.diag_offset;
     if (last_c < 0) continue;
-    const int64_t cnt = last_c / bn + 1;
+    const int64_t cnt = last_c / ts.col_step + 1;
     per += cnt < ts.tiles_n ? cnt : ts.tiles_n;
   }
   ts.per_matrix = per;
@@ -589,7 +594,11 @@ template <int BN>
 int launch_tc_bn(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
   CUtensorMap mp, mq;
   if (!make_map(&mp, g.P, g.K, g.m, g.batch, g.ldp, g.pstride, kBM)) return CHOL_ERR_UNSUPPORTED;
-  if (!make_map(&mq, g.Q, g.K, g.ncols, g.batch, g.ldq, g.qstride, BN))
+  // with a column-cyclic map Q's rows reach the last mapped row
+  const int64_t qrows = g.cmap_block ? (g.ncols - 1) + ((g.ncols - 1) / g.cmap_block) *
+                                                          (g.cmap_stride - g.cmap_block) + 1
+                                     : g.ncols;
+  if (!make_map(&mq, g.Q, g.K, qrows, g.batch, g.ldq, g.qstride, BN))
     return CHOL_ERR_UNSUPPORTED;
   return launch_tc_maps<BN>(g, mp, mq, TmaOrigin{0, 0, 0, 0}, q, pdl, status);
 }
@@ -645,6 +654,10 @@ int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMat
 }
 
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
+  if (g.cmap_block) {
+    if (g.cmap_block != 256 || g.cmap_stride < 256 || g.cmap_stride % 256) return CHOL_ERR_UNSUPPORTED;
+    return launch_tc_bn<256>(g, q, pdl, status);
+  }
   if (g.ncols <= 64) return launch_tc_bn<64>(g, q, pdl, status);
   if (g.ncols <= 128) return launch_tc_bn<128>(g, q, pdl, status);
   return launch_tc_bn<256>(g, q, pdl, status);

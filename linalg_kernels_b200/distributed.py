@@ -5,13 +5,15 @@ cholesky/cholesky.py:5692-5802). Here one process per GPU holds the column block
 ``t = rank, rank + P, rank + 2P, ...`` (block width ``bs``, default 256) of the matrix,
 row-major in a local ``(n, n_local)`` tensor. For every block column ``j``:
 
-1. its owner factors the panel ``L[j*bs:, j*bs:(j+1)*bs]`` in place: four 64-wide steps of
-   diagonal factor + inverse (``chol_block_potrf_f32``), panel solve ``X <- X T^T`` and
-   in-panel update (``chol_gemm_nt_f32``, tensor cores);
+1. its owner factors the panel ``L[j*bs:, j*bs:(j+1)*bs]`` in place with one
+   ``chol_panel_potrf_f32`` call (64-wide left-looking steps: diagonal factor + inverse,
+   panel solve ``X <- X T^T``, on tensor cores);
 2. the factored panel (rows ``j*bs .. n``, ``bs`` columns, at most 32 MiB at n = 32768) is
    packed contiguously and broadcast by NCCL from the owner into every rank's receive
    buffer (local memory; no kernel reads another GPU's memory);
-3. every rank applies ``C -= P P^T`` (lower tiles, K = bs) to each of its blocks ``t > j``.
+3. every rank applies ``C -= P P^T`` (lower tiles, K = bs) to all of its blocks ``t > j`` in
+   one ``chol_gemm_nt_cyclic_f32`` launch (the GEMM maps local column blocks to their
+   global columns, so masking and Q's rows follow the cyclic layout).
 
 Look-ahead: the owner of block ``j+1`` first updates that block with panel ``j``, factors
 it and starts its broadcast; only then does every rank update its remaining blocks with
@@ -113,6 +115,34 @@ class CudaOps:
             ctypes.c_void_p(info.data_ptr()) if info is not None else None, self._q())
         _lib.check(st, "chol_block_potrf_f32")
 
+    def panel_potrf(self, panel: torch.Tensor, tinv: torch.Tensor, info: torch.Tensor | None):
+        """Factor a tall panel view (m x w, element (0,0) on the diagonal) in place."""
+        m, w = panel.shape
+        st = self.lib.chol_panel_potrf_f32(
+            ctypes.c_void_p(panel.data_ptr()), _rowmajor(panel), m, w,
+            ctypes.c_void_p(tinv.data_ptr()),
+            ctypes.c_void_p(info.data_ptr()) if info is not None else None, self._q())
+        _lib.check(st, "chol_panel_potrf_f32")
+
+    def cyclic_update(self, c: torch.Tensor, p: torch.Tensor, block: int, stride: int):
+        """c -= p q^T over cyclically stored column blocks (q = rows of p at the mapped
+        global columns), lower part only; element (0,0) of c is on the diagonal."""
+        m, nc = c.shape
+        k = p.shape[1]
+        if block == 256:
+            st = self.lib.chol_gemm_nt_cyclic_f32(
+                ctypes.c_void_p(c.data_ptr()), _rowmajor(c), m, nc, k,
+                ctypes.c_void_p(p.data_ptr()), _rowmajor(p),
+                ctypes.c_void_p(p.data_ptr()), _rowmajor(p), -1.0, 1.0, 0, 1, block, stride,
+                self._q())
+            if st != _lib.CHOL_ERR_UNSUPPORTED:
+                _lib.check(st, "chol_gemm_nt_cyclic_f32")
+                return
+        for b in range(0, nc, block):  # one launch per block
+            w = min(block, nc - b)
+            r = (b // block) * stride
+            self.gemm_nt(c[r:, b:b + w], p[r:], p[r:r + w], -1.0, 1.0, True)
+
     def gemm_nt(self, c: torch.Tensor, p: torch.Tensor, q: torch.Tensor, alpha: float,
                 beta: float, lower_only: bool):
         """c = alpha * p q^T + beta * c; lower_only keeps elements with col <= row."""
@@ -127,31 +157,21 @@ class CudaOps:
 
 
 def _factor_panel(local: torch.Tensor, lay: CyclicLayout, t: int, ops, tinv, info):
-    """Owner: factor block column t in place (rows t*bs..n of its local columns), 64-wide
-    steps, left-looking inside the panel."""
-    n, bs = lay.n, lay.bs
-    c0, w, lc = t * bs, lay.width(t), lay.local_col(t)
-    for kk in range(0, w, 64):
-        kb = min(64, w - kk)
-        r = c0 + kk  # global row (and column) of this 64-block
-        col = lc + kk  # its local column
-        if kk > 0:
-            prev = local[r:, lc:col]
-            ops.gemm_nt(local[r:, col:col + kb], prev, prev[:kb], -1.0, 1.0, True)
-        ops.potrf_block(local[r:r + kb, col:col + kb], tinv, info)
-        if n - r - kb <= 0:
-            continue
-        x = local[r + kb:, col:col + kb]
-        ops.gemm_nt(x, x, tinv[:kb, :kb], 1.0, 0.0, False)
+    """Owner: factor block column t in place (rows t*bs..n of its local columns)."""
+    c0, w, lc = t * lay.bs, lay.width(t), lay.local_col(t)
+    ops.panel_potrf(local[c0:, lc:lc + w], tinv, info)
 
 
-def _update_block(local: torch.Tensor, lay: CyclicLayout, t: int, j: int, panel, ops):
-    """local block t -= panel_j-contribution (rows t*bs..n, lower part)."""
+def _update_blocks(local: torch.Tensor, lay: CyclicLayout, blocks: list[int], j: int, panel,
+                   ops):
+    """Owned blocks `blocks` (consecutive in this rank's storage) -= panel_j P P^T, lower
+    part, in one call: local column block b stands for global block blocks[0] + b*world."""
     bs = lay.bs
-    c0, w, lc = t * bs, lay.width(t), lay.local_col(t)
-    off = c0 - j * bs  # panel row of global row c0
-    p = panel[off:]
-    ops.gemm_nt(local[c0:, lc:lc + w], p, p[:w], -1.0, 1.0, True)
+    t0 = blocks[0]
+    c0, lc0 = t0 * bs, lay.local_col(t0)
+    width = sum(lay.width(t) for t in blocks)
+    p = panel[c0 - j * bs:]
+    ops.cyclic_update(local[c0:, lc0:lc0 + width], p, bs, bs * lay.world)
 
 
 def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=None, ops=None,
@@ -195,12 +215,12 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
         work = None
         if nxt < nb:
             if lay.owner(nxt) == lay.rank:
-                _update_block(local, lay, nxt, j, panel, ops)
+                _update_blocks(local, lay, [nxt], j, panel, ops)
                 _factor_panel(local, lay, nxt, ops, tinv, info)
             work = publish(nxt)
-        for t in lay.owned():
-            if t > nxt:
-                _update_block(local, lay, t, j, panel, ops)
+        rest = [t for t in lay.owned() if t > nxt]
+        if rest:
+            _update_blocks(local, lay, rest, j, panel, ops)
     return local
 
 

@@ -23,6 +23,21 @@ class CpuOps:
         tinv.fill_diagonal_(1.0)
         tinv[:kb, :kb] = torch.linalg.inv(l)
 
+    def panel_potrf(self, panel, tinv, info):
+        w = panel.shape[1]
+        d = panel[:w]
+        l = torch.linalg.cholesky(torch.tril(d) + torch.tril(d, -1).T)
+        d.copy_(l)
+        if panel.shape[0] > w:
+            panel[w:] = torch.linalg.solve_triangular(l, panel[w:].T, upper=False).T
+
+    def cyclic_update(self, c, p, block, stride):
+        nc = c.shape[1]
+        for b in range(0, nc, block):
+            w = min(block, nc - b)
+            r = (b // block) * stride
+            self.gemm_nt(c[r:, b:b + w], p[r:], p[r:r + w], -1.0, 1.0, True)
+
     def gemm_nt(self, c, p, q, alpha, beta, lower_only):
         new = alpha * (p @ q.T) + (beta * c if beta != 0.0 else 0.0)
         if lower_only:

@@ -90,3 +90,29 @@ def test_cyclic_two_ranks_nccl(tmp_path):
     l_or, _ = oracle.potrf(a.numpy())
     res = oracle.check_factor(a.numpy(), l, l_ref=l_or, cond=cond.numpy())
     assert res["ok"], res
+
+
+@pytest.mark.parametrize("world,nblk", [(1, 3), (2, 3), (3, 2)])
+def test_cyclic_gemm_matches_per_block(world, nblk):
+    """chol_gemm_nt_cyclic_f32 (one launch over cyclically stored blocks) equals the same
+    update done block by block in FP64."""
+    from linalg_kernels_b200.distributed import CudaOps
+
+    bs, k = 256, 256
+    stride = bs * world
+    m = (nblk - 1) * stride + bs + 100  # rows below the first block's diagonal
+    g = torch.Generator(device=DEV).manual_seed(world * 10 + nblk)
+    p = torch.randn(m, k, device=DEV, generator=g)
+    c0 = torch.randn(m, nblk * bs - 40, device=DEV, generator=g)
+    c = c0.clone()
+    CudaOps(torch.device(DEV)).cyclic_update(c, p, bs, stride)
+    torch.cuda.synchronize()
+    want = c0.double().clone()
+    for b in range(nblk):
+        w = min(bs, c0.shape[1] - b * bs)
+        r = b * stride
+        upd = want[r:, b * bs:b * bs + w] - p[r:].double() @ p[r:r + w].double().T
+        keep = torch.ones_like(upd, dtype=torch.bool).tril()
+        want[r:, b * bs:b * bs + w] = torch.where(keep, upd, want[r:, b * bs:b * bs + w])
+    err = (c.double() - want).abs().max().item()
+    assert err < 8 * k * 2.0 ** -22 * 25.0, err

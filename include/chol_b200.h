@@ -126,6 +126,9 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   TMA, FP32 FMA otherwise; default), 1 = FP32 FMA only, 2 = tensor cores only.
  */
 #define CHOL_OPT_GEMM_ENGINE 1
+/*   CHOL_OPT_FUSED_PANEL: 1 = one fused launch per 64-wide step of the blocked path (update,
+ *   diagonal factor and solve in one tcgen05 kernel), 0 = three launches (default). */
+#define CHOL_OPT_FUSED_PANEL 2
 CHOL_API int chol_set_option(int option, int value);
 
 /*

@@ -77,9 +77,14 @@ bool overlaps_partially(const float* a, const float* b, int64_t count) {
   return a0 < b0 + bytes && b0 < a0 + bytes;
 }
 
+// Workspace of the blocked path: the inverse diagonal blocks (64 x 64 floats per matrix,
+// used by the FP32-FMA schedule and the building blocks) followed by one arrival counter
+// per matrix for the fused panel step.
 size_t blocked_workspace(int64_t batch, int64_t n) {
   if (n <= 64) return 0;
-  return size_t(batch) * kBlock * kBlock * sizeof(float);
+  const size_t tinv = size_t(batch) * kBlock * kBlock * sizeof(float);
+  const size_t counters = (size_t(batch) * sizeof(unsigned) + 255) & ~size_t(255);
+  return tinv + counters;
 }
 
 // Tensor-core GEMMs of one call share tensor maps built once over L and the inverse blocks;
@@ -100,18 +105,30 @@ int gemm_on(const GemmArgs& g, const BlockedMaps& bm, const TcMatrixMaps& pm,
 
 int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, float* Tws,
                 cudaStream_t q) {
-  int st = launch_copy_lower(A, L, batch, n, q, true);
-  if (st) return st;
+  unsigned int* counters = reinterpret_cast<unsigned int*>(Tws + batch * kBlock * kBlock);
   const int64_t mstride = n * n;
   BlockedMaps bm;
+  alignas(64) unsigned char pmap[128];
   if (g_gemm_engine != 1)
     bm.ok = tc_make_matrix_maps(L, n, n, n, batch, mstride, &bm.L) &&
-            tc_make_matrix_maps(Tws, kBlock, kBlock, kBlock, batch, kBlock * kBlock, &bm.T);
+            tc_make_matrix_maps(Tws, kBlock, kBlock, kBlock, batch, kBlock * kBlock, &bm.T) &&
+            panel_make_map(pmap, L, n, batch);
+  if (bm.ok && g_fused_panel &&
+      cudaMemsetAsync(counters, 0, size_t(batch) * sizeof(unsigned), q) != cudaSuccess)
+    return CHOL_ERR_LAUNCH;
+  int st = launch_copy_lower(A, L, batch, n, q, true);
+  if (st) return st;
   const int64_t NB = outer_width(n);
   for (int64_t K0 = 0; K0 < n; K0 += NB) {
     const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
     for (int64_t k = K0; k < K0 + KB; k += kBlock) {
       const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
+      if (bm.ok && g_fused_panel) {
+        // one fused launch: left-looking update, diagonal factor + inverse, panel solve
+        st = launch_panel_step(pmap, L, n, batch, k, kb, K0, info, counters, q);
+        if (st) return st;
+        continue;
+      }
       if (k > K0) {
         // left-looking inside the outer panel: block column k receives the updates of the
         // panel's already factored columns [K0, k) in one GEMM (K = k - K0)
@@ -189,13 +206,17 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
 }
 
 // Launch count of run_blocked for (batch, n); keep in step with the schedule above.
-int64_t blocked_launches(int64_t n) {
+int64_t blocked_launches(int64_t n, bool fused) {
   int64_t count = 1;  // copy_lower
   const int64_t NB = outer_width(n);
   for (int64_t K0 = 0; K0 < n; K0 += NB) {
     const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
     for (int64_t k = K0; k < K0 + KB; k += kBlock) {
       const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
+      if (fused) {
+        count += 1;
+        continue;
+      }
       if (k > K0) count += 1;  // left-looking panel update
       count += 1;              // diagonal block
       if (n - k - kb > 0) count += 1;  // panel solve
@@ -234,10 +255,15 @@ int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int
 }
 
 int prepare_kernels(int /*device*/) {
-  return prepare_tc() == cudaSuccess ? CHOL_OK : CHOL_ERR_DEVICE;
+  return (prepare_tc() == cudaSuccess && prepare_panel() == cudaSuccess) ? CHOL_OK
+                                                                          : CHOL_ERR_DEVICE;
 }
 
 int g_gemm_engine = 0;
+// Fused panel step (chol_panel.cu) instead of the three-launch step. Off by default: its
+// redundant per-CTA diagonal factor measured slower than the three launches on every
+// BASELINE shape (b640n512 2.85 vs 1.28 ms, n = 16384 18.8 vs 18.3 ms).
+int g_fused_panel = 0;
 
 int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl) {
   if (g.m <= 0 || g.ncols <= 0) return CHOL_OK;
@@ -320,13 +346,20 @@ int chol_potrf_batched_f32(const float* A, float* L, int64_t batch, int64_t n, i
 int64_t chol_launch_count(int64_t batch, int64_t n) {
   if (batch <= 0 || n <= 0) return 0;
   if (n <= 64) return 1;
-  return blocked_launches(n);
+  // the fused panel step runs when the tensor-core engine is allowed and rows are
+  // 16-byte multiples (the usual case: n % 4 == 0)
+  return blocked_launches(n, g_fused_panel && g_gemm_engine != 1 && n % 4 == 0);
 }
 
 int chol_set_option(int option, int value) {
   if (option == CHOL_OPT_GEMM_ENGINE) {
     if (value < 0 || value > 2) return CHOL_ERR_INVALID_ARG;
     g_gemm_engine = value;
+    return CHOL_OK;
+  }
+  if (option == CHOL_OPT_FUSED_PANEL) {
+    if (value < 0 || value > 1) return CHOL_ERR_INVALID_ARG;
+    g_fused_panel = value;
     return CHOL_OK;
   }
   return CHOL_ERR_INVALID_ARG;

@@ -150,9 +150,17 @@ int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMat
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status);
 cudaError_t prepare_tc();
 int read_and_clear_status(int* out);
+// Device address of the status word (for kernels in other translation units).
+int* device_status_ptr();
+// Fused 64-wide panel step (chol_panel.cu).
+cudaError_t prepare_panel();
+bool panel_make_map(void* map128, const float* L, int64_t n, int64_t batch);
+int launch_panel_step(const void* map128, float* L, int64_t n, int64_t batch, int64_t k,
+                      int64_t kb, int64_t K0, int* info, unsigned int* counters, cudaStream_t q);
 // Engine choice for the NT-GEMM: 0 auto (tensor cores when the operands allow TMA), 1 FP32
 // FMA only, 2 tensor cores only (CHOL_ERR_UNSUPPORTED where TMA cannot be used).
 extern int g_gemm_engine;
+extern int g_fused_panel;
 int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl);
 
 }  // namespace chol

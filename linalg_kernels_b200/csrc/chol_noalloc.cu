@@ -6,8 +6,9 @@
 // acceptable. chol_potrf_batched_f32 grows a cached workspace with cudaMalloc, and
 // chol_potrf_batched_ws_f32 needs the caller to allocate one. This entry point instead
 // takes the only scratch the factorisation needs (the inverse of each 64 x 64 diagonal
-// block of the blocked path, 16 KiB per matrix with n > 64) from one fixed file-scope
-// device array, g_noalloc_scratch, of kNoAllocScratchBytes (4 MiB). Every GPU that loads
+// block of the blocked path, 16 KiB per matrix with n > 64, and a 4-byte arrival counter per
+// matrix) from one fixed file-scope device array, g_noalloc_scratch, of kNoAllocScratchBytes
+// (4 MiB + 64 KiB). Every GPU that loads
 // the library holds that array until the process exits.
 //
 // Host code may not pass the array's name to a kernel: on the host it is only a stand-in
@@ -15,8 +16,9 @@
 // cudaGetSymbolAddress, with that device current, by the first call on the device; that
 // first call should therefore come before any stream capture.
 //
-// All calls share the one array and it keeps the previous call's contents. Nothing in it
-// needs to start at zero (each diagonal block's inverse is written before it is read),
+// All calls share the one array and it keeps the previous call's contents. The counters
+// must start at zero and every call clears them first (cudaMemsetAsync on its queue); the
+// inverse blocks are written before they are read,
 // but calls whose work overlaps on the GPU (different queues, or different host threads
 // without ordering) race on it and must be serialised by the caller.
 #include <mutex>
@@ -26,7 +28,8 @@
 namespace chol {
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB: 256 matrices with n > 64
+// 4 MiB of inverse blocks + 64 KiB of per-matrix counters: 256 matrices with n > 64
+constexpr size_t kNoAllocScratchBytes = (size_t(4) << 20) + (size_t(64) << 10);
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

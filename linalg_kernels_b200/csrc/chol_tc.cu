@@ -27,7 +27,7 @@
 
 #include <mutex>
 
-#include "chol_common.cuh"
+#include "chol_tc_ptx.cuh"
 
 namespace chol {
 
@@ -35,8 +35,9 @@ __device__ int g_device_status = 0;
 
 namespace {
 
+using namespace tcx;
+
 constexpr int kBM = 128;
-constexpr int kBK = 32;  // fp32 elements of K per stage = one 128-byte swizzle row
 constexpr int kThreads = 320;  // producer, MMA, 4 converter warps, 4 epilogue warps
 
 template <int BN>
@@ -53,180 +54,54 @@ struct TcCfg {
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
 };
 
-// ------------------------------- PTX wrappers ---------------------------------------
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
-
-// Bounded wait for the completion of phase `parity`. Returns false (and records the
-// timeout in the status word) if it does not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
-      atomicExch(status, CHOL_ERR_WAIT_TIMEOUT);
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
-                                            int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// K-major operand, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(const void* smem_tile) {
-  const uint32_t addr = smem_u32(smem_tile);
-  uint64_t d = 0;
-  d |= uint64_t((addr >> 4) & 0x3FFF);  // start address
-  d |= uint64_t(1) << 16;               // leading byte offset (unused for SW128 K-major)
-  d |= uint64_t(1024 >> 4) << 32;       // stride byte offset: 8 rows x 128 B
-  d |= uint64_t(1) << 46;               // descriptor version (sm_100)
-  d |= uint64_t(2) << 61;               // SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor: D f32, A/B tf32, K-major both, N, M = 128.
-template <int BN>
-__device__ __forceinline__ uint32_t tf32_idesc() {
-  return (1u << 4)                       // D format f32
-         | (2u << 7)                     // A format tf32
-         | (2u << 10)                    // B format tf32
-         | (uint32_t(BN >> 3) << 17)     // N >> 3
-         | (uint32_t(kBM >> 4) << 24);   // M >> 4
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// hi/lo split of one 16-byte chunk: lo to the twin buffer; hi written back in place when
-// WRITE_HI (otherwise the tensor core's own TF32 conversion of x must equal hi).
-template <bool WRITE_HI>
-__device__ __forceinline__ void split4(float4* hi_p, float4* lo_p) {
-  const float4 x = *hi_p;
-  float4 h, l;
-  h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
-  h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
-  h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
-  h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
-  l.x = x.x - h.x;
-  l.y = x.y - h.y;
-  l.z = x.z - h.z;
-  l.w = x.w - h.w;
-  if (WRITE_HI) *hi_p = h;
-  *lo_p = l;
-}
-
 // Tile enumeration: per matrix, row tiles tm = 0..TM-1 and, in row tm, column tiles
 // tn = 0..last(tm) where last(tm) = TN-1 for a full GEMM and the last tile touching the
 // lower part (c <= r + diag_offset) otherwise. Tiles of one matrix are numbered row by row.
+constexpr int kRowTable = 256;  // row tiles covered by the prefix table (kernel parameter): m <= 32768
+
 struct TileSpace {
   int64_t tiles_m, tiles_n, per_matrix, total;
   int64_t diag_offset;
   int lower_only;
   int bn;
   int64_t col_step;  // global columns between consecutive column tiles (bn, or the cyclic stride)
+  int use_table;     // row_start[] valid (tiles_m <= kRowTable)
+  int32_t row_start[kRowTable + 1];  // index of tile (tm, 0) within a matrix
   __device__ __forceinline__ int64_t row_count(int64_t tm) const {
     if (!lower_only) return tiles_n;
-    const int64_t last_c = tm * kBM + kBM - 1 + diag_offset;
+    const int64_t last_c = tm * 128 + 127 + diag_offset;
     if (last_c < 0) return 0;
     const int64_t cnt = last_c / col_step + 1;
     return cnt < tiles_n ? cnt : tiles_n;
   }
+  // Row tile holding in-matrix tile index r, searching from row tm0 (r >= row_start(tm0)).
+  __device__ __forceinline__ void locate(int64_t r, int64_t& tm, int64_t& base) const {
+    if (!lower_only) {
+      tm = r / tiles_n;
+      base = tm * tiles_n;
+      return;
+    }
+    if (use_table) {
+      int lo = int(tm), hi = int(tiles_m) - 1;  // invariant: row_start[lo] <= r
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (row_start[mid] <= r)
+          lo = mid;
+        else
+          hi = mid - 1;
+      }
+      tm = lo;
+      base = row_start[lo];
+      return;
+    }
+    for (;;) {
+      const int64_t cnt = row_count(tm);
+      if (r < base + cnt) return;
+      base += cnt;
+      ++tm;
+    }
+  }
 };
-
-// Origin of the view inside the tensor maps (element coordinates: x = column, y = row).
-struct TmaOrigin {
-  int px, py, qx, qy;
-};
-
-// Split of chunk i of a 128B-swizzled K-major tile (8 chunks of 4 floats per row; the
-// chunk at physical slot p of row r holds logical columns 4 * (p ^ (r & 7)) .. +3) with
-// columns >= kval set to zero in both the raw buffer and lo.
-__device__ __forceinline__ void split4_masked(float4* hi_p, float4* lo_p, int i, int kval) {
-  const int row = i >> 3, phys = i & 7;
-  const int col0 = 4 * (phys ^ (row & 7));
-  float4 x = *hi_p;
-  if (col0 + 0 >= kval) x.x = 0.f;
-  if (col0 + 1 >= kval) x.y = 0.f;
-  if (col0 + 2 >= kval) x.z = 0.f;
-  if (col0 + 3 >= kval) x.w = 0.f;
-  *hi_p = x;
-  split4<false>(hi_p, lo_p);
-}
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -294,38 +169,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     c.valid = c.t < ts.total;
     if (!c.valid) return;
     c.mi = c.t / ts.per_matrix;
-    int64_t r = c.t - c.mi * ts.per_matrix;
+    const int64_t r = c.t - c.mi * ts.per_matrix;
     c.tm = 0;
     c.row_base = 0;
-    for (;;) {
-      const int64_t cnt = ts.row_count(c.tm);
-      if (r < cnt) break;
-      r -= cnt;
-      c.row_base += cnt;
-      ++c.tm;
-    }
-    c.tn = r;
+    ts.locate(r, c.tm, c.row_base);
+    c.tn = r - c.row_base;
   };
   auto next_tile = [&](Cursor& c) {
     c.t += gridDim.x;
     c.valid = c.t < ts.total;
     if (!c.valid) return;
     const int64_t mi = c.t / ts.per_matrix;
-    int64_t r = c.t - mi * ts.per_matrix;
+    const int64_t r = c.t - mi * ts.per_matrix;
     if (mi != c.mi) {
       c.mi = mi;
       c.tm = 0;
       c.row_base = 0;
     }
-    r -= c.row_base;
-    for (;;) {
-      const int64_t cnt = ts.row_count(c.tm);
-      if (r < cnt) break;
-      r -= cnt;
-      c.row_base += cnt;
-      ++c.tm;
-    }
-    c.tn = r;
+    ts.locate(r, c.tm, c.row_base);
+    c.tn = r - c.row_base;
   };
 
   if (warp == 0) {
@@ -354,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = tf32_idesc<BN>();
+      const uint32_t idesc = tf32_idesc<kBM, BN>();
       Cursor c;
       first_tile(c);
       uint32_t kt = 0, it = 0;
@@ -555,8 +417,10 @@ TileSpace make_tiles(const GemmArgs& g, int bn) {
   ts.lower_only = g.lower_only;
   ts.bn = bn;
   ts.col_step = g.cmap_block ? g.cmap_stride : bn;
+  ts.use_table = ts.lower_only && ts.tiles_m <= kRowTable;
   int64_t per = 0;
   for (int64_t tm = 0; tm < ts.tiles_m; ++tm) {
+    if (ts.use_table) ts.row_start[tm] = int32_t(per);
     if (!ts.lower_only) {
       per += ts.tiles_n;
       continue;
@@ -566,6 +430,8 @@ TileSpace make_tiles(const GemmArgs& g, int bn) {
     const int64_t cnt = last_c / ts.col_step + 1;
     per += cnt < ts.tiles_n ? cnt : ts.tiles_n;
   }
+  if (ts.use_table) ts.row_start[ts.tiles_m] = int32_t(per);
+  if (per > 0x7fffffffLL) ts.use_table = 0;
   ts.per_matrix = per;
   ts.total = per * g.batch;
   return ts;
@@ -679,6 +545,19 @@ cudaError_t prepare_tc() {
   if ((e = set_tc_smem<256>()) != cudaSuccess) return e;
   resolve_encode();
   return cudaSuccess;
+}
+
+int* device_status_ptr() {
+  static int* ptrs[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) == cudaSuccess) ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
 }
 
 int read_and_clear_status(int* out) {

@@ -197,3 +197,15 @@ def test_building_blocks_against_torch():
     assert st == 0
     torch.cuda.synchronize()
     assert (l[:, kb:, :kb] - want_x).abs().max().item() < 1e-4
+
+
+@pytest.mark.parametrize("name", ["b64n256", "b640n512", "b60n1024"])
+def test_fused_panel_step_option(name):
+    """The fused one-launch panel step (CHOL_OPT_FUSED_PANEL) gives a factor within the
+    same bounds as the default three-launch step."""
+    lib = _lib.load()
+    lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, 1)
+    try:
+        _check_full_config(name, batch=8)
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, 0)

@@ -89,6 +89,32 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         return lib
 
 
+_pyext = None
+
+
+def potrf_ws(a: int, l: int, batch: int, n: int, info: int, ws: int, ws_bytes: int,
+             queue: int) -> int:
+    """chol_potrf_batched_ws_f32 through the CPython fast-call binding (_cholpy), falling
+    back to ctypes when the binding is not built. Integer arguments, 0 for NULL."""
+    global _pyext
+    if _pyext is None:
+        load()
+        try:
+            from . import _cholpy  # type: ignore
+
+            _pyext = _cholpy.potrf_ws
+        except ImportError:
+            lib = load()
+
+            def _via_ctypes(*args):
+                return lib.chol_potrf_batched_ws_f32(*[x if x else None for x in args[:2]],
+                                                     args[2], args[3], args[4] or None,
+                                                     args[5] or None, args[6], args[7] or None)
+
+            _pyext = _via_ctypes
+    return _pyext(a, l, batch, n, info, ws, ws_bytes, queue)
+
+
 def strerror(status: int) -> str:
     try:
         return load().chol_strerror(int(status)).decode()
@@ -105,4 +131,10 @@ def current_queue(device) -> int:
     """Raw handle of torch's current CUDA queue on ``device`` (0 = legacy default)."""
     import torch
 
-    return int(torch.cuda.current_stream(device).cuda_stream)
+    idx = device.index if isinstance(device, torch.device) else device
+    if idx is None:
+        idx = torch.cuda.current_device()
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:  # no Python queue object per call
+        return int(raw(idx))
+    return int(torch.cuda.current_stream(idx).cuda_stream)

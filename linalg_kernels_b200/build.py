@@ -50,7 +50,8 @@ def sources() -> list[Path]:
 
 def _digest() -> str:
     h = hashlib.sha256()
-    files = sources() + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    files = (sources() + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.c"))
+             + sorted(INCLUDE.glob("*.h")))
     for f in files:
         h.update(f.name.encode())
         h.update(f.read_bytes())
@@ -83,8 +84,26 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
     os.replace(tmp, LIB_PATH)
+    _build_pyext(verbose)
     STAMP.write_text(digest + "\n")
     return LIB_PATH
+
+
+def _build_pyext(verbose: bool) -> Path:
+    """gcc the CPython fast-call binding (csrc/chol_pyext.c) against libchol_b200.so."""
+    import sysconfig
+
+    suffix = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
+    out = PKG_DIR / ("_cholpy" + suffix)
+    tmp = out.with_name(out.name + ".tmp")
+    cmd = ["gcc", "-O2", "-shared", "-fPIC", "-I", sysconfig.get_paths()["include"],
+           "-I", str(INCLUDE), str(CSRC / "chol_pyext.c"), "-o", str(tmp),
+           "-L", str(PKG_DIR), "-lchol_b200", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, out)
+    return out
 
 
 def main(argv: list[str] | None = None) -> int:

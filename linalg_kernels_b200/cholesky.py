@@ -19,8 +19,6 @@ Non-SPD input is not an error here, as in the reference (``check_errors=False``)
 
 from __future__ import annotations
 
-import ctypes
-
 import torch
 
 from . import _lib
@@ -28,9 +26,16 @@ from . import _lib
 __all__ = ["custom_kernel", "cholesky_ex", "cholesky", "workspace_bytes"]
 
 
+_F32 = torch.float32
+
+
 def _prepare_input(data: torch.Tensor) -> tuple[torch.Tensor, int, int]:
     if not isinstance(data, torch.Tensor):
         raise TypeError("custom_kernel expects a torch.Tensor")
+    shape = data.shape
+    if data.is_cuda and data.dtype is _F32 and len(shape) == 3 and shape[1] == shape[2] \
+            and data.is_contiguous():
+        return data, int(shape[0]), int(shape[2])  # the common (b, n, n) case
     if not data.is_cuda:
         raise TypeError("custom_kernel runs on the GPU only: move the input to a CUDA device "
                         "(this build has no CPU fallback)")
@@ -52,6 +57,19 @@ def workspace_bytes(batch: int, n: int) -> int:
     return int(_lib.load().chol_workspace_bytes(int(batch), int(n)))
 
 
+_ws_bytes: dict[tuple[int, int], int] = {}
+
+
+def _workspace_bytes(lib, batch: int, n: int) -> int:
+    key = (batch, n)
+    need = _ws_bytes.get(key)
+    if need is None:
+        need = int(lib.chol_workspace_bytes(batch, n))
+        if len(_ws_bytes) < 4096:
+            _ws_bytes[key] = need
+    return need
+
+
 def _factor(data: torch.Tensor, want_info: bool):
     data, batch, n = _prepare_input(data)
     lib = _lib.load()
@@ -60,16 +78,22 @@ def _factor(data: torch.Tensor, want_info: bool):
         else None
     if batch == 0 or n == 0:
         return out, info
-    with torch.cuda.device(data.device):
-        need = int(lib.chol_workspace_bytes(batch, n))
-        ws = torch.empty(need, dtype=torch.uint8, device=data.device) if need else None
-        queue = _lib.current_queue(data.device)
-        status = lib.chol_potrf_batched_ws_f32(
-            ctypes.c_void_p(data.data_ptr()), ctypes.c_void_p(out.data_ptr()), batch, n,
-            ctypes.c_void_p(info.data_ptr()) if info is not None else None,
-            ctypes.c_void_p(ws.data_ptr()) if ws is not None else None, need,
-            ctypes.c_void_p(queue))
-    _lib.check(status, "chol_potrf_batched_ws_f32")
+    dev = data.device.index
+    if dev != torch.cuda.current_device():
+        with torch.cuda.device(dev):
+            return _launch(lib, data, out, info, batch, n, dev)
+    return _launch(lib, data, out, info, batch, n, dev)
+
+
+def _launch(lib, data, out, info, batch, n, dev):
+    need = _workspace_bytes(lib, batch, n)
+    ws = torch.empty(need, dtype=torch.uint8, device=data.device) if need else None
+    status = _lib.potrf_ws(
+        data.data_ptr(), out.data_ptr(), batch, n,
+        info.data_ptr() if info is not None else 0,
+        ws.data_ptr() if ws is not None else 0, need, _lib.current_queue(dev))
+    if status:
+        _lib.check(status, "chol_potrf_batched_ws_f32")
     return out, info
 
 

@@ -109,15 +109,15 @@ __global__ void __launch_bounds__(128)
   __syncthreads();
 
   if (tid < 32) {
-    float2 a[2][32];
+    uint64_t a[2][32];
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       const float* rp = tile + (s * 32 + tid) * kPBLD;
 #pragma unroll
       for (int q = 0; q < (s + 1) * 8; ++q) {
-        const float4 v = *reinterpret_cast<const float4*>(rp + 4 * q);
-        a[s][2 * q] = make_float2(v.x, v.y);
-        a[s][2 * q + 1] = make_float2(v.z, v.w);
+        const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(rp + 4 * q);
+        a[s][2 * q] = v.x;
+        a[s][2 * q + 1] = v.y;
       }
     }
     warp_potrf_rows<64>(a, col, tid);
@@ -130,11 +130,10 @@ __global__ void __launch_bounds__(128)
       for (int q = 0; q < kPB / 4; ++q) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (4 * q < (s + 1) * 32) {
-          const float2 lo = a[s][2 * q], hi = a[s][2 * q + 1];
-          v.x = (4 * q + 0 <= i) ? lo.x : 0.f;
-          v.y = (4 * q + 1 <= i) ? lo.y : 0.f;
-          v.z = (4 * q + 2 <= i) ? hi.x : 0.f;
-          v.w = (4 * q + 3 <= i) ? hi.y : 0.f;
+          v.x = (4 * q + 0 <= i) ? lo_of(a[s][2 * q]) : 0.f;
+          v.y = (4 * q + 1 <= i) ? hi_of(a[s][2 * q]) : 0.f;
+          v.z = (4 * q + 2 <= i) ? lo_of(a[s][2 * q + 1]) : 0.f;
+          v.w = (4 * q + 3 <= i) ? hi_of(a[s][2 * q + 1]) : 0.f;
         }
         *reinterpret_cast<float4*>(rp + 4 * q) = v;
       }

@@ -218,15 +218,15 @@ __global__ void __launch_bounds__(kPS_Threads, 2)
 
     // ---- factor the diagonal block (one warp, registers) ----
     if (warp == 2) {
-      float2 ar[2][32];
+      uint64_t ar[2][32];
 #pragma unroll
       for (int s = 0; s < 2; ++s) {
         const float* rp = S + (s * 32 + lane) * kPS_SLD;
 #pragma unroll
         for (int qq = 0; qq < (s + 1) * 8; ++qq) {
-          const float4 v = *reinterpret_cast<const float4*>(rp + 4 * qq);
-          ar[s][2 * qq] = make_float2(v.x, v.y);
-          ar[s][2 * qq + 1] = make_float2(v.z, v.w);
+          const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(rp + 4 * qq);
+          ar[s][2 * qq] = v.x;
+          ar[s][2 * qq + 1] = v.y;
         }
       }
       warp_potrf_rows<64>(ar, colbuf, lane);
@@ -239,11 +239,10 @@ __global__ void __launch_bounds__(kPS_Threads, 2)
         for (int qq = 0; qq < 16; ++qq) {
           float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
           if (4 * qq < (s + 1) * 32) {
-            const float2 lo = ar[s][2 * qq], hi = ar[s][2 * qq + 1];
-            v.x = (4 * qq + 0 <= i) ? lo.x : 0.f;
-            v.y = (4 * qq + 1 <= i) ? lo.y : 0.f;
-            v.z = (4 * qq + 2 <= i) ? hi.x : 0.f;
-            v.w = (4 * qq + 3 <= i) ? hi.y : 0.f;
+            v.x = (4 * qq + 0 <= i) ? lo_of(ar[s][2 * qq]) : 0.f;
+            v.y = (4 * qq + 1 <= i) ? hi_of(ar[s][2 * qq]) : 0.f;
+            v.z = (4 * qq + 2 <= i) ? lo_of(ar[s][2 * qq + 1]) : 0.f;
+            v.w = (4 * qq + 3 <= i) ? hi_of(ar[s][2 * qq + 1]) : 0.f;
           }
           *reinterpret_cast<float4*>(rp + 4 * qq) = v;
         }

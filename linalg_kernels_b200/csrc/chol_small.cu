@@ -10,6 +10,12 @@
 // memory (row stride NP+4: conflict-free 128-bit row reads), factored in registers by
 // warp_potrf_rows<NP>, staged back and written as full rows (upper triangle as exact
 // zeros) with coalesced 128-bit streaming stores.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
 #include "chol_warp.cuh"
 
 namespace chol {
@@ -18,31 +24,56 @@ namespace {
 
 constexpr int kSmallWarps = 4;
 
+// Lanes per matrix for each padded size: 8 lanes x 4 rows for n <= 32 (four matrices per
+// warp share each per-column step), a full warp x 2 rows for n = 64.
+template <int NP>
+constexpr int small_lpm() {
+  return NP >= 64 ? 32 : (NP >= 32 ? 8 : (NP >= 16 ? 8 : NP));
+}
+template <int NP>
+using SmallShape = WarpShape<NP, small_lpm<NP>()>;
+
+// Staging tile of one matrix: NP rows of stride NP+4 floats for the loads, reused as
+// NP/32 128B-swizzled 32-column tiles for the tensor store; rounded to 1 KiB (the swizzled
+// layout needs 1024-byte aligned tiles).
+template <int NP>
+constexpr int small_tile_floats() {
+  return ((NP * (NP + 4) * 4 + 1023) / 1024) * 1024 / 4;
+}
 template <int NP>
 constexpr size_t small_smem_bytes() {
-  return size_t(kSmallWarps) * WarpShape<NP>::MPW * (size_t(NP) * (NP + 4) + 2 * NP) * 4;
+  return size_t(kSmallWarps) * SmallShape<NP>::MPW *
+             (size_t(small_tile_floats<NP>()) + SmallShape<NP>::COLS) * 4 + 1024;
+}
+// The tensor-store path covers n = 32 and n = 64 (rows of 128-byte multiples).
+template <int NP>
+constexpr bool small_tma_store() {
+  return NP >= 32;
 }
 
 // FULL: n == NP and 16-byte aligned rows (vector path). Otherwise scalar loads with
 // identity padding of rows/columns n..NP-1.
 template <int NP, bool FULL>
-__global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 8 : 1)
+__global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 3 : 1)
     small_potrf_kernel(const float* __restrict__ A, float* __restrict__ L, int64_t batch, int n,
-                       int* __restrict__ info) {
-  constexpr int LPM = WarpShape<NP>::LPM;
-  constexpr int R = WarpShape<NP>::R;
-  constexpr int MPW = WarpShape<NP>::MPW;
+                       int* __restrict__ info, const __grid_constant__ CUtensorMap out_map) {
+  constexpr int LPM = SmallShape<NP>::LPM;
+  constexpr int R = SmallShape<NP>::R;
+  constexpr int MPW = SmallShape<NP>::MPW;
   constexpr int LDS = NP + 4;
-  constexpr int TILE = NP * LDS;
-  extern __shared__ float4 smem_raw[];
-  float* smem = reinterpret_cast<float*>(smem_raw);
+  constexpr int TILE = small_tile_floats<NP>();
+  constexpr bool TMA_OUT = FULL && small_tma_store<NP>();
+  extern __shared__ __align__(1024) float4 smem_raw[];
+  float* smem = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                         ~uintptr_t(1023));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int grp = lane / LPM;
   const int gl = lane % LPM;
   float* stage = smem + size_t(warp) * MPW * TILE;
-  float* col = smem + size_t(kSmallWarps) * MPW * TILE + size_t(warp * MPW + grp) * 2 * NP;
+  float* col = smem + size_t(kSmallWarps) * MPW * TILE +
+               size_t(warp * MPW + grp) * SmallShape<NP>::COLS;
   const int64_t mbase = (int64_t(blockIdx.x) * kSmallWarps + warp) * MPW;
   if (FULL) n = NP;
 
@@ -85,20 +116,20 @@ __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 8 : 1)
   __syncwarp();
 
   // ---- rows to registers (column pairs) ----
-  float2 a[R][NP / 2];
+  uint64_t a[R][NP / 2];
   const float* mst = stage + grp * TILE;
 #pragma unroll
   for (int s = 0; s < R; ++s) {
     const float* rp = mst + (s * LPM + gl) * LDS;
 #pragma unroll
     for (int q = 0; q < (s + 1) * LPM / 4; ++q) {
-      const float4 v = *reinterpret_cast<const float4*>(rp + 4 * q);
-      a[s][2 * q] = make_float2(v.x, v.y);
-      a[s][2 * q + 1] = make_float2(v.z, v.w);
+      const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(rp + 4 * q);
+      a[s][2 * q] = v.x;
+      a[s][2 * q + 1] = v.y;
     }
   }
 
-  warp_potrf_rows<NP>(a, col, gl);
+  warp_potrf_rows<NP, LPM>(a, col, gl);
   __syncwarp();
 
   // ---- registers to staging, strict upper part as exact zeros ----
@@ -114,17 +145,25 @@ __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 8 : 1)
     for (int q = 0; q < NP / 4; ++q) {
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (4 * q < (s + 1) * LPM) {
-        const float2 lo = a[s][2 * q], hi = a[s][2 * q + 1];
-        v.x = (4 * q + 0 <= i) ? lo.x : 0.f;
-        v.y = (4 * q + 1 <= i) ? lo.y : 0.f;
-        v.z = (4 * q + 2 <= i) ? hi.x : 0.f;
-        v.w = (4 * q + 3 <= i) ? hi.y : 0.f;
+        const float lx = lo_of(a[s][2 * q]), ly = hi_of(a[s][2 * q]);
+        const float hx = lo_of(a[s][2 * q + 1]), hy = hi_of(a[s][2 * q + 1]);
+        v.x = (4 * q + 0 <= i) ? lx : 0.f;
+        v.y = (4 * q + 1 <= i) ? ly : 0.f;
+        v.z = (4 * q + 2 <= i) ? hx : 0.f;
+        v.w = (4 * q + 3 <= i) ? hy : 0.f;
         if (4 * q <= i && i < 4 * q + 4) {
-          const float dg = (i & 2) ? ((i & 1) ? hi.y : hi.x) : ((i & 1) ? lo.y : lo.x);
+          const float dg = (i & 2) ? ((i & 1) ? hy : hx) : ((i & 1) ? ly : lx);
           bad[s] = !(dg > 0.f);
         }
       }
-      *reinterpret_cast<float4*>(rp + 4 * q) = v;
+      if (TMA_OUT) {
+        // 128B-swizzled 32-column tiles: chunk qh of row i at slot qh ^ (i & 7)
+        const int h = q >> 3, qh = q & 7;
+        float* tile = stage + grp * TILE + h * (NP * 32);
+        *reinterpret_cast<float4*>(tile + i * 32 + ((qh ^ (i & 7)) << 2)) = v;
+      } else {
+        *reinterpret_cast<float4*>(rp + 4 * q) = v;
+      }
     }
   }
   int fail = 0;
@@ -136,9 +175,26 @@ __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 8 : 1)
   }
   __syncwarp();
 
-  // ---- store: full rows. Vector path: one bulk async copy per row, issued by the lane
-  // that holds the row; scalar path: coalesced 4-byte stores. ----
-  if (FULL) {
+  // ---- store. n = 32/64: one tensor store per 32-column half of each matrix from the
+  // swizzled tiles; smaller full sizes: one bulk copy per row; otherwise 4-byte stores ----
+  if (TMA_OUT) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane < MPW) {
+      const int64_t m = mbase + lane;
+      if (m < batch) {
+        const float* base = stage + lane * TILE;
+#pragma unroll
+        for (int h = 0; h < NP / 32; ++h)
+          asm volatile(
+              "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::
+                  "l"(reinterpret_cast<uint64_t>(&out_map)),
+              "r"(h * 32), "r"(0), "r"(int(m)), "r"(smem_u32(base + h * (NP * 32)))
+              : "memory");
+      }
+      bulk_store_wait_read();
+    }
+  } else if (FULL) {
     fence_proxy_async_smem();
     __syncwarp();
 #pragma unroll 1
@@ -170,21 +226,85 @@ __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 8 : 1)
   }
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 g_small_enc = nullptr;
+
+// Store map over L as (n, n, batch) with 32-column x NP-row boxes, 128-byte swizzle.
+bool small_out_map(CUtensorMap* map, float* L, int64_t batch, int n, int np) {
+  if (g_small_enc == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) !=
+            cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess)
+      return false;
+    g_small_enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  cuuint64_t dims[3] = {cuuint64_t(n), cuuint64_t(n), cuuint64_t(batch)};
+  cuuint64_t strides[2] = {cuuint64_t(n) * 4, cuuint64_t(n) * cuuint64_t(n) * 4};
+  cuuint32_t box[3] = {32, cuuint32_t(np), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_small_enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, L, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Encoded store maps keyed by (L, batch, n): torch's caching allocator hands the same
+// output addresses back in steady state, so most calls skip the host-side encode.
+struct OutMapCache {
+  static constexpr int kSlots = 16;
+  struct Slot {
+    float* L = nullptr;
+    int64_t batch = 0;
+    int n = 0, np = 0;
+    alignas(64) CUtensorMap map;
+  } slots[kSlots];
+  int next = 0;
+  std::mutex mu;
+};
+
+bool cached_out_map(CUtensorMap* out, float* L, int64_t batch, int n, int np) {
+  static OutMapCache cache;
+  std::lock_guard<std::mutex> lock(cache.mu);
+  for (auto& s : cache.slots) {
+    if (s.L == L && s.batch == batch && s.n == n && s.np == np) {
+      *out = s.map;
+      return true;
+    }
+  }
+  auto& s = cache.slots[cache.next];
+  if (!small_out_map(&s.map, L, batch, n, np)) {
+    s.L = nullptr;
+    return false;
+  }
+  s.L = L;
+  s.batch = batch;
+  s.n = n;
+  s.np = np;
+  cache.next = (cache.next + 1) % OutMapCache::kSlots;
+  *out = s.map;
+  return true;
+}
+
 template <int NP>
 int launch_np(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q) {
-  constexpr int MPC = kSmallWarps * WarpShape<NP>::MPW;
+  constexpr int MPC = kSmallWarps * SmallShape<NP>::MPW;
   const int64_t blocks = (batch + MPC - 1) / MPC;
   if (blocks > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
   const size_t smem = small_smem_bytes<NP>();
   const bool full = (n == NP) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0) &&
                     ((reinterpret_cast<uintptr_t>(L) & 15) == 0);
+  alignas(64) CUtensorMap map;
+  memset(&map, 0, sizeof(map));
+  if (full && small_tma_store<NP>() && !cached_out_map(&map, L, batch, n, NP))
+    return CHOL_ERR_UNSUPPORTED;
   cudaError_t e;
   if (full)
     e = launch_pdl(small_potrf_kernel<NP, true>, dim3(unsigned(blocks)), dim3(kSmallWarps * 32),
-                   smem, q, true, A, L, batch, n, info);
+                   smem, q, true, A, L, batch, n, info, map);
   else
     e = launch_pdl(small_potrf_kernel<NP, false>, dim3(unsigned(blocks)),
-                   dim3(kSmallWarps * 32), smem, q, true, A, L, batch, n, info);
+                   dim3(kSmallWarps * 32), smem, q, true, A, L, batch, n, info, map);
   return status_from(e);
 }
 

@@ -2,10 +2,9 @@
 //
 // Layout: a group of LPM = min(NP, 32) lanes owns one matrix; lane gl of the group holds
 // rows i = s*LPM + gl (s = 0..R-1, R = NP/LPM). Row i of slot s is kept as column pairs
-// a[s][p] = (A[i][2p], A[i][2p+1]) for p < (s+1)*LPM/2: slot s never needs columns past
-// its last row, so the per-slot register bound is static and the triangular shape costs
-// no predicated work beyond one slot width. Pairs sit in aligned 64-bit registers, which
-// is what the packed f32x2 FMA reads and writes.
+// a[s][p] = (A[i][2p], A[i][2p+1]) for p < (s+1)*LPM/2 in 64-bit registers: slot s never
+// needs columns past its last row, so the per-slot register bound is static, and the packed
+// f32x2 FMA reads and writes the pairs with no packing moves.
 //
 // Algorithm (LAPACK xPOTF2, right-looking form; the reference's small kernels use the
 // same recurrence, cholesky/b4096n32/DESIGN.md:13-21, cholesky/cholesky.py:294-387):
@@ -27,12 +26,16 @@
 
 namespace chol {
 
-template <int NP>
+// LPM lanes share one matrix (default min(NP, 32)); fewer lanes per matrix means more
+// matrices per warp sharing every per-column instruction (shuffle, rsqrt, broadcast).
+template <int NP, int LPM_ = (NP < 32 ? NP : 32)>
 struct WarpShape {
-  static constexpr int LPM = NP < 32 ? NP : 32;  // lanes per matrix
+  static constexpr int LPM = LPM_;               // lanes per matrix
   static constexpr int R = NP / LPM;             // rows per lane
   static constexpr int MPW = 32 / LPM;           // matrices per warp
+  static constexpr int COLS = 2 * NP + 8;        // per-group column buffer stride (floats)
   static_assert(NP >= 4 && NP <= 64 && (NP & (NP - 1)) == 0, "NP must be 4..64, power of 2");
+  static_assert(LPM >= 4 && LPM <= 32 && NP % LPM == 0, "LPM");
 };
 
 __device__ __forceinline__ float rsqrt_approx(float x) {
@@ -41,25 +44,25 @@ __device__ __forceinline__ float rsqrt_approx(float x) {
   return y;
 }
 
+// Row storage: a[s][p] holds columns 2p (low half) and 2p+1 (high half) of one row as a
+// 64-bit register pair; the packed FMA consumes and produces these pairs directly.
 template <int NP>
-__device__ __forceinline__ float pair_get(const float2 (&row)[NP / 2], int k) {
-  return (k & 1) ? row[k >> 1].y : row[k >> 1].x;
+__device__ __forceinline__ float pair_get(const uint64_t (&row)[NP / 2], int k) {
+  return (k & 1) ? hi_of(row[k >> 1]) : lo_of(row[k >> 1]);
 }
 template <int NP>
-__device__ __forceinline__ void pair_set(float2 (&row)[NP / 2], int k, float v) {
-  if (k & 1)
-    row[k >> 1].y = v;
-  else
-    row[k >> 1].x = v;
+__device__ __forceinline__ void pair_set(uint64_t (&row)[NP / 2], int k, float v) {
+  const uint64_t cur = row[k >> 1];
+  row[k >> 1] = (k & 1) ? pack2(lo_of(cur), v) : pack2(v, hi_of(cur));
 }
 
 // col: this group's 2*NP floats of shared memory (16-byte aligned).
-template <int NP>
-__device__ __forceinline__ void warp_potrf_rows(float2 (&a)[WarpShape<NP>::R][NP / 2], float* col,
+template <int NP, int LPM_ = (NP < 32 ? NP : 32)>
+__device__ __forceinline__ void warp_potrf_rows(uint64_t (&a)[NP / LPM_][NP / 2], float* col,
                                                 int gl) {
-  constexpr int LPM = WarpShape<NP>::LPM;
-  constexpr int R = WarpShape<NP>::R;
-  float dnext = a[0][0].x;
+  constexpr int LPM = LPM_;
+  constexpr int R = NP / LPM;
+  float dnext = lo_of(a[0][0]);
 #pragma unroll
   for (int j = 0; j < NP; ++j) {
     const float d = __shfl_sync(0xffffffffu, dnext, j % LPM, LPM);
@@ -85,25 +88,26 @@ __device__ __forceinline__ void warp_potrf_rows(float2 (&a)[WarpShape<NP>::R][NP
     __syncwarp();
     if (j + 1 < NP) {
       const int q0 = (j + 1) >> 2;
-      float2 cv[NP / 2];
+      uint64_t cv[NP / 2];
 #pragma unroll
       for (int q = q0; q < NP / 4; ++q) {
-        const float4 v = *reinterpret_cast<const float4*>(cb + 4 * q);
-        cv[2 * q] = make_float2(v.x, v.y);
-        cv[2 * q + 1] = make_float2(v.z, v.w);
+        const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(cb + 4 * q);
+        cv[2 * q] = v.x;
+        cv[2 * q + 1] = v.y;
       }
 #pragma unroll
       for (int s = 0; s < R; ++s) {
         if ((s + 1) * LPM - 1 <= j) continue;
         const float nl = -lv[s];
         int p0 = (j + 1) >> 1;
-        if ((j + 1) & 1) {  // odd first column: scalar fma, then whole pairs
-          a[s][p0].y = fmaf(nl, cv[p0].y, a[s][p0].y);
+        if ((j + 1) & 1) {  // odd first column: scalar fma on the high half, then whole pairs
+          const uint64_t cur = a[s][p0];
+          a[s][p0] = pack2(lo_of(cur), fmaf(nl, hi_of(cv[p0]), hi_of(cur)));
           ++p0;
         }
-        const float2 nl2 = make_float2(nl, nl);
+        const uint64_t nl2 = pack2(nl, nl);
 #pragma unroll
-        for (int p = p0; p < (s + 1) * LPM / 2; ++p) a[s][p] = ffma2(nl2, cv[p], a[s][p]);
+        for (int p = p0; p < (s + 1) * LPM / 2; ++p) a[s][p] = ffma2_u64(nl2, cv[p], a[s][p]);
       }
     }
   }

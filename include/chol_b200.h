@@ -127,8 +127,12 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  */
 #define CHOL_OPT_GEMM_ENGINE 1
 /*   CHOL_OPT_FUSED_PANEL: 1 = one fused launch per 64-wide step of the blocked path (update,
- *   diagonal factor and solve in one tcgen05 kernel), 0 = three launches (default). */
+ *   diagonal factor and solve in one tcgen05 kernel), 0 = three launches, -1 = automatic
+ *   (default: fused for few large matrices, n > 1024 and one wave of CTAs per step). */
 #define CHOL_OPT_FUSED_PANEL 2
+/*   CHOL_OPT_OUTER_WIDTH: width of the outer panels of the blocked path (multiple of 64;
+ *   0 = default: n for n <= 1024, else 512). */
+#define CHOL_OPT_OUTER_WIDTH 3
 CHOL_API int chol_set_option(int option, int value);
 
 /*

@@ -25,8 +25,12 @@ namespace {
 
 constexpr int64_t kBlock = 64;
 
+int g_outer_width = 0;  // 0: default (n for n <= 1024, else 512)
+
 int64_t outer_width(int64_t n) {
-  // n <= 1024: one outer panel (plain right-looking with 64-wide steps); larger: 512.
+  // n <= 1024: one outer panel (left-looking 64-wide steps); larger: 512-wide panels with
+  // a rank-512 trailing update between them.
+  if (g_outer_width > 0 && g_outer_width % 64 == 0) return n <= g_outer_width ? n : g_outer_width;
   return n <= 1024 ? n : 512;
 }
 
@@ -78,13 +82,23 @@ bool overlaps_partially(const float* a, const float* b, int64_t count) {
 }
 
 // Workspace of the blocked path: the inverse diagonal blocks (64 x 64 floats per matrix,
-// used by the FP32-FMA schedule and the building blocks) followed by one arrival counter
-// per matrix for the fused panel step.
-size_t blocked_workspace(int64_t batch, int64_t n) {
+// used by the FP32-FMA schedule and the building blocks), one arrival counter per matrix
+// for the fused panel step, and (when there is a trailing update, n > outer width) the
+// low TF32 parts of one outer panel (n x NB floats per matrix) so that the trailing GEMM
+// loads them instead of splitting in shared memory. Only the first two are required.
+size_t blocked_workspace_min(int64_t batch, int64_t n) {
   if (n <= 64) return 0;
   const size_t tinv = size_t(batch) * kBlock * kBlock * sizeof(float);
   const size_t counters = (size_t(batch) * sizeof(unsigned) + 255) & ~size_t(255);
   return tinv + counters;
+}
+size_t blocked_lo_bytes(int64_t batch, int64_t n) {
+  const int64_t NB = outer_width(n);
+  if (n <= 64 || NB >= n || n % 4) return 0;
+  return size_t(batch) * size_t(n) * size_t(NB) * sizeof(float);
+}
+size_t blocked_workspace(int64_t batch, int64_t n) {
+  return blocked_workspace_min(batch, n) + blocked_lo_bytes(batch, n);
 }
 
 // Tensor-core GEMMs of one call share tensor maps built once over L and the inverse blocks;
@@ -104,17 +118,26 @@ int gemm_on(const GemmArgs& g, const BlockedMaps& bm, const TcMatrixMaps& pm,
 }
 
 int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, float* Tws,
-                cudaStream_t q) {
+                size_t ws_bytes, cudaStream_t q) {
   unsigned int* counters = reinterpret_cast<unsigned int*>(Tws + batch * kBlock * kBlock);
   const int64_t mstride = n * n;
+  const size_t lo_bytes = blocked_lo_bytes(batch, n);
+  float* lo = (lo_bytes && ws_bytes >= blocked_workspace_min(batch, n) + lo_bytes)
+                  ? reinterpret_cast<float*>(reinterpret_cast<char*>(Tws) +
+                                             blocked_workspace_min(batch, n))
+                  : nullptr;
   BlockedMaps bm;
+  TcMatrixMaps lomap;
   alignas(64) unsigned char pmap[128];
+  const int64_t NBw = outer_width(n);
   if (g_gemm_engine != 1)
     bm.ok = tc_make_matrix_maps(L, n, n, n, batch, mstride, &bm.L) &&
             tc_make_matrix_maps(Tws, kBlock, kBlock, kBlock, batch, kBlock * kBlock, &bm.T) &&
             panel_make_map(pmap, L, n, batch);
-  if (bm.ok && g_fused_panel &&
-      cudaMemsetAsync(counters, 0, size_t(batch) * sizeof(unsigned), q) != cudaSuccess)
+  if (!bm.ok || (lo && !tc_make_matrix_maps(lo, n, NBw, NBw, batch, n * NBw, &lomap)))
+    lo = nullptr;
+  const bool fused = bm.ok && use_fused(batch, n);
+  if (fused && cudaMemsetAsync(counters, 0, size_t(batch) * sizeof(unsigned), q) != cudaSuccess)
     return CHOL_ERR_LAUNCH;
   int st = launch_copy_lower(A, L, batch, n, q, true);
   if (st) return st;
@@ -123,7 +146,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
     const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
     for (int64_t k = K0; k < K0 + KB; k += kBlock) {
       const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
-      if (bm.ok && g_fused_panel) {
+      if (fused) {
         // one fused launch: left-looking update, diagonal factor + inverse, panel solve
         st = launch_panel_step(pmap, L, n, batch, k, kb, K0, info, counters, q);
         if (st) return st;
@@ -198,7 +221,15 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       t.diag_offset = 0;
       t.lower_only = 1;
       t.batch = batch;
-      st = gemm_on(t, bm, bm.L, bm.L, q);
+      if (lo != nullptr && KB == NBw && g_gemm_engine != 1) {
+        // low parts of the panel rows below it, computed once, read by every tile
+        st = launch_tf32_lo(L + (K0 + KB) * n + K0, n, lo + (K0 + KB) * NBw, NBw, rest, KB, batch,
+                            mstride, n * NBw, q);
+        if (st) return st;
+        st = launch_gemm_tc_mapped_lo(t, bm.L, bm.L, lomap, 0, q, true);
+      } else {
+        st = gemm_on(t, bm, bm.L, bm.L, q);
+      }
       if (st) return st;
     }
   }
@@ -221,7 +252,7 @@ int64_t blocked_launches(int64_t n, bool fused) {
       count += 1;              // diagonal block
       if (n - k - kb > 0) count += 1;  // panel solve
     }
-    if (n - K0 - KB > 0) count += 1;
+    if (n - K0 - KB > 0) count += (n % 4 == 0 && NB < n) ? 2 : 1;  // (+ lo pass)
   }
   return count;
 }
@@ -238,9 +269,9 @@ int check_common(const float* A, float* L, int64_t batch, int64_t n) {
 int potrf_impl(const float* A, float* L, int64_t batch, int64_t n, int* info, void* ws,
                size_t ws_bytes, cudaStream_t q) {
   if (n <= 64) return launch_small(A, L, batch, int(n), info, q);
-  if (ws == nullptr || ws_bytes < blocked_workspace(batch, n)) return CHOL_ERR_WORKSPACE;
+  if (ws == nullptr || ws_bytes < blocked_workspace_min(batch, n)) return CHOL_ERR_WORKSPACE;
   if (batch > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
-  return run_blocked(A, L, batch, n, info, static_cast<float*>(ws), q);
+  return run_blocked(A, L, batch, n, info, static_cast<float*>(ws), ws_bytes, q);
 }
 
 }  // namespace
@@ -248,6 +279,9 @@ int potrf_impl(const float* A, float* L, int64_t batch, int64_t n, int* info, vo
 int prepare_device_checked(int dev) { return prepare_device(dev); }
 int check_potrf_args(const float* A, float* L, int64_t batch, int64_t n) {
   return check_common(A, L, batch, n);
+}
+size_t workspace_min_bytes(int64_t batch, int64_t n) {
+  return (batch <= 0 || n <= 0) ? 0 : blocked_workspace_min(batch, n);
 }
 int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int* info, void* ws,
                          size_t ws_bytes, cudaStream_t q) {
@@ -260,10 +294,18 @@ int prepare_kernels(int /*device*/) {
 }
 
 int g_gemm_engine = 0;
-// Fused panel step (chol_panel.cu) instead of the three-launch step. Off by default: its
-// redundant per-CTA diagonal factor measured slower than the three launches on every
-// BASELINE shape (b640n512 2.85 vs 1.28 ms, n = 16384 18.8 vs 18.3 ms).
+// Fused panel step (chol_panel.cu) instead of the three-launch step: 1 always, 0 never,
+// -1 auto. Auto currently means never: measured per step, the fused kernel (one warp factors
+// the diagonal block while five wait, ~28k instructions per CTA) is slower than the three
+// launches (n = 16384: 17.5 vs 16.5 ms; b640n512: 2.85 vs 1.3 ms).
 int g_fused_panel = 0;
+
+bool use_fused(int64_t batch, int64_t n) {
+  if (g_fused_panel >= 0) return g_fused_panel == 1;
+  (void)batch;
+  (void)n;
+  return false;
+}
 
 int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl) {
   if (g.m <= 0 || g.ncols <= 0) return CHOL_OK;
@@ -348,7 +390,7 @@ int64_t chol_launch_count(int64_t batch, int64_t n) {
   if (n <= 64) return 1;
   // the fused panel step runs when the tensor-core engine is allowed and rows are
   // 16-byte multiples (the usual case: n % 4 == 0)
-  return blocked_launches(n, g_fused_panel && g_gemm_engine != 1 && n % 4 == 0);
+  return blocked_launches(n, use_fused(batch, n) && g_gemm_engine != 1 && n % 4 == 0);
 }
 
 int chol_set_option(int option, int value) {
@@ -357,8 +399,13 @@ int chol_set_option(int option, int value) {
     g_gemm_engine = value;
     return CHOL_OK;
   }
+  if (option == CHOL_OPT_OUTER_WIDTH) {
+    if (value < 0 || value % 64) return CHOL_ERR_INVALID_ARG;
+    g_outer_width = value;
+    return CHOL_OK;
+  }
   if (option == CHOL_OPT_FUSED_PANEL) {
-    if (value < 0 || value > 1) return CHOL_ERR_INVALID_ARG;
+    if (value < -1 || value > 1) return CHOL_ERR_INVALID_ARG;
     g_fused_panel = value;
     return CHOL_OK;
   }

@@ -141,6 +141,9 @@ struct GemmArgs {
 // Entry-point plumbing shared by the C-ABI files (chol_api.cu).
 int prepare_device_checked(int dev);
 int check_potrf_args(const float* A, float* L, int64_t batch, int64_t n);
+// Smallest workspace a call can run with (the blocked path then splits every operand in
+// shared memory instead of reading precomputed low parts).
+size_t workspace_min_bytes(int64_t batch, int64_t n);
 int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int* info, void* ws,
                          size_t ws_bytes, cudaStream_t q);
 
@@ -169,6 +172,10 @@ bool tc_make_matrix_maps(const float* base, int64_t rows, int64_t cols, int64_t 
                          int64_t bstride, TcMatrixMaps* maps);
 int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
                           cudaStream_t q, bool pdl);
+int launch_gemm_tc_mapped_lo(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
+                             const TcMatrixMaps& lm, int64_t lk, cudaStream_t q, bool pdl);
+int launch_tf32_lo(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows,
+                   int64_t cols, int64_t batch, int64_t sstride, int64_t dstride, cudaStream_t q);
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status);
 cudaError_t prepare_tc();
 int read_and_clear_status(int* out);
@@ -183,6 +190,7 @@ int launch_panel_step(const void* map128, float* L, int64_t n, int64_t batch, in
 // FMA only, 2 tensor cores only (CHOL_ERR_UNSUPPORTED where TMA cannot be used).
 extern int g_gemm_engine;
 extern int g_fused_panel;
+bool use_fused(int64_t batch, int64_t n);
 int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl);
 
 }  // namespace chol

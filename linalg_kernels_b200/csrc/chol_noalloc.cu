@@ -70,7 +70,7 @@ extern "C" int chol_potrf_batched_noalloc_f32(const float* A, float* L, int64_t 
                                               int* info, void* queue) {
   int st = check_potrf_args(A, L, batch, n);
   if (st || batch == 0 || n == 0) return st;
-  const size_t need = chol_workspace_bytes(batch, n);
+  const size_t need = workspace_min_bytes(batch, n);
   if (need > kNoAllocScratchBytes) return CHOL_ERR_SCRATCH_LIMIT;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;

@@ -26,7 +26,7 @@ namespace {
 using namespace tcx;
 
 constexpr int kPS_Threads = 192;  // producer, MMA, 4 converter/epilogue warps
-constexpr int kPS_Stages = 2;
+constexpr int kPS_Stages = 3;
 constexpr int kPS_ABytes = 128 * kBK * 4;           // 16 KB: 128 rows x 32 floats
 constexpr int kPS_StageBytes = 2 * kPS_ABytes;      // A and its lo twin
 constexpr int kPS_SLD = 68;                         // factor/solve tile stride (floats)

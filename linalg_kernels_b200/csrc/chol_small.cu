@@ -28,7 +28,7 @@ constexpr int kSmallWarps = 4;
 // warp share each per-column step), a full warp x 2 rows for n = 64.
 template <int NP>
 constexpr int small_lpm() {
-  return NP >= 64 ? 32 : (NP >= 32 ? 8 : (NP >= 16 ? 8 : NP));
+  return NP >= 64 ? 16 : (NP >= 32 ? 8 : (NP >= 16 ? 8 : NP));
 }
 template <int NP>
 using SmallShape = WarpShape<NP, small_lpm<NP>()>;

@@ -103,10 +103,15 @@ struct TileSpace {
   }
 };
 
-template <int BN>
+// PRELO: the low parts of P and Q come from precomputed buffers (tmPlo / tmQlo, same row
+// coordinates, K from org.lpx / org.lqx): four TMA boxes per stage, no split pass, the
+// MMA waits on TMA completion directly. Otherwise converter warps write lo in shared memory.
+template <int BN, bool PRELO>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
-                   GemmArgs g, TileSpace ts, TmaOrigin org, int* status) {
+                   const __grid_constant__ CUtensorMap tmPlo,
+                   const __grid_constant__ CUtensorMap tmQlo, GemmArgs g, TileSpace ts,
+                   TmaOrigin org, int* status) {
   using Cfg = TcCfg<BN>;
   constexpr int S = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -144,6 +149,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&tmP);
     prefetch_map(&tmQ);
+    if (PRELO) {
+      prefetch_map(&tmPlo);
+      prefetch_map(&tmQlo);
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -207,9 +216,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[s], Cfg::A_BYTES + Cfg::B_BYTES);
+          mbar_expect_tx(&full[s], (PRELO ? 2 : 1) * (Cfg::A_BYTES + Cfg::B_BYTES));
           tma_load_3d(stA(s), &tmP, org.px + k * kBK, y0, zc, &full[s]);
           tma_load_3d(stB(s), &tmQ, org.qx + k * kBK, y1, zc, &full[s]);
+          if (PRELO) {
+            tma_load_3d(stAlo(s), &tmPlo, org.lpx + k * kBK, y0, zc, &full[s]);
+            tma_load_3d(stBlo(s), &tmQlo, org.lqx + k * kBK, y1, zc, &full[s]);
+          }
         }
       }
     }
@@ -229,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < num_k; ++k, ++kt) {
           const int s = int(kt % S);
           const uint32_t ph = (kt / S) & 1u;
-          if (!mbar_wait(&conv[s], ph, st_word)) {
+          if (!mbar_wait(PRELO ? &full[s] : &conv[s], ph, st_word)) {
             ok = false;
             break;
           }
@@ -250,6 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 6) {
     // ---------------- converters: lo = x - trunc_tf32(x) ----------------
+    if (!PRELO) {
     const int ct = threadIdx.x - 64;
     Cursor c;
     first_tile(c);
@@ -283,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[s]);
       }
+    }
     }
   } else {
     // ---------------- epilogue: TMEM -> C ----------------
@@ -441,7 +456,8 @@ int g_num_sms = 0;
 
 template <int BN>
 int launch_tc_maps(const GemmArgs& g, const CUtensorMap& mp, const CUtensorMap& mq,
-                   TmaOrigin org, cudaStream_t q, bool pdl, int* status) {
+                   TmaOrigin org, cudaStream_t q, bool pdl, int* status,
+                   const CUtensorMap* mplo = nullptr, const CUtensorMap* mqlo = nullptr) {
   using Cfg = TcCfg<BN>;
   const TileSpace ts = make_tiles(g, BN);
   if (ts.total == 0) return CHOL_OK;
@@ -452,8 +468,11 @@ int launch_tc_maps(const GemmArgs& g, const CUtensorMap& mp, const CUtensorMap& 
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
   const int64_t ctas = ts.total < sms ? ts.total : sms;
-  return status_from(launch_pdl(tc_gemm_kernel<BN>, dim3(unsigned(ctas)), dim3(kThreads),
-                                Cfg::SMEM, q, pdl, mp, mq, g, ts, org, status));
+  if (mplo != nullptr && mqlo != nullptr)
+    return status_from(launch_pdl(tc_gemm_kernel<BN, true>, dim3(unsigned(ctas)), dim3(kThreads),
+                                  Cfg::SMEM, q, pdl, mp, mq, *mplo, *mqlo, g, ts, org, status));
+  return status_from(launch_pdl(tc_gemm_kernel<BN, false>, dim3(unsigned(ctas)), dim3(kThreads),
+                                Cfg::SMEM, q, pdl, mp, mq, mp, mq, g, ts, org, status));
 }
 
 template <int BN>
@@ -466,7 +485,7 @@ int launch_tc_bn(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
                                      : g.ncols;
   if (!make_map(&mq, g.Q, g.K, qrows, g.batch, g.ldq, g.qstride, BN))
     return CHOL_ERR_UNSUPPORTED;
-  return launch_tc_maps<BN>(g, mp, mq, TmaOrigin{0, 0, 0, 0}, q, pdl, status);
+  return launch_tc_maps<BN>(g, mp, mq, TmaOrigin{0, 0, 0, 0, 0, 0}, q, pdl, status);
 }
 
 }  // namespace
@@ -506,7 +525,7 @@ int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMat
   if (po < 0 || qo < 0 || g.ldp != pm.ld || g.ldq != qm.ld) return CHOL_ERR_INVALID_ARG;
   if (g.batch > 1 && (g.pstride != pm.bstride || g.qstride != qm.bstride))
     return CHOL_ERR_INVALID_ARG;
-  TmaOrigin org{int(po % pm.ld), int(po / pm.ld), int(qo % qm.ld), int(qo / qm.ld)};
+  TmaOrigin org{int(po % pm.ld), int(po / pm.ld), int(qo % qm.ld), int(qo / qm.ld), 0, 0};
   if ((org.px & 3) || (org.qx & 3)) return CHOL_ERR_INVALID_ARG;  // TMA x must be 16-byte aligned
   const CUtensorMap& mp = *reinterpret_cast<const CUtensorMap*>(pm.p128);
   if (g.ncols <= 64)
@@ -517,6 +536,27 @@ int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMat
                                pdl, nullptr);
   return launch_tc_maps<256>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q256), org, q, pdl,
                              nullptr);
+}
+
+// As launch_gemm_tc_mapped with the low parts of P and Q read from a precomputed buffer
+// (maps lm, rows indexed like P/Q's matrix, K origin lk) instead of split in the kernel.
+int launch_gemm_tc_mapped_lo(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
+                             const TcMatrixMaps& lm, int64_t lk, cudaStream_t q, bool pdl) {
+  const int64_t po = g.P - pm.base, qo = g.Q - qm.base;
+  if (po < 0 || qo < 0 || g.ldp != pm.ld || g.ldq != qm.ld) return CHOL_ERR_INVALID_ARG;
+  TmaOrigin org{int(po % pm.ld), int(po / pm.ld), int(qo % qm.ld), int(qo / qm.ld), int(lk),
+                int(lk)};
+  if ((org.px & 3) || (org.qx & 3) || (lk & 3)) return CHOL_ERR_INVALID_ARG;
+  const CUtensorMap& mp = *reinterpret_cast<const CUtensorMap*>(pm.p128);
+  const CUtensorMap& mpl = *reinterpret_cast<const CUtensorMap*>(lm.p128);
+  if (g.ncols <= 64)
+    return launch_tc_maps<64>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q64), org, q, pdl,
+                              nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q64));
+  if (g.ncols <= 128)
+    return launch_tc_maps<128>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q128), org, q,
+                               pdl, nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q128));
+  return launch_tc_maps<256>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q256), org, q, pdl,
+                             nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q256));
 }
 
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
@@ -531,8 +571,35 @@ int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
 
 template <int BN>
 cudaError_t set_tc_smem() {
-  return cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(TcCfg<BN>::SMEM));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(tc_gemm_kernel<BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               int(TcCfg<BN>::SMEM));
+}
+
+// lo = x - trunc_tf32(x) for a rows x cols view (float4 columns; cols % 4 == 0).
+__global__ void __launch_bounds__(256) tf32_lo_kernel(const float* __restrict__ src, int64_t lds,
+                                                      float* __restrict__ dst, int64_t ldd,
+                                                      int64_t rows, int64_t cols4, int64_t batch,
+                                                      int64_t sstride, int64_t dstride) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t total = batch * rows * cols4;
+  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t c4 = t % cols4;
+    const int64_t rr = t / cols4;
+    const int64_t r = rr % rows, m = rr / rows;
+    const float4 x = *reinterpret_cast<const float4*>(src + m * sstride + r * lds + 4 * c4);
+    float4 l;
+    l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+    l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+    l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+    l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+    *reinterpret_cast<float4*>(dst + m * dstride + r * ldd + 4 * c4) = l;
+  }
 }
 
 cudaError_t prepare_tc() {
@@ -545,6 +612,18 @@ cudaError_t prepare_tc() {
   if ((e = set_tc_smem<256>()) != cudaSuccess) return e;
   resolve_encode();
   return cudaSuccess;
+}
+
+int launch_tf32_lo(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows,
+                   int64_t cols, int64_t batch, int64_t sstride, int64_t dstride, cudaStream_t q) {
+  if (rows <= 0 || cols <= 0 || batch <= 0) return CHOL_OK;
+  if (cols % 4 || lds % 4 || ldd % 4) return CHOL_ERR_UNSUPPORTED;
+  const int64_t work = batch * rows * (cols / 4);
+  int64_t blocks = (work + 255) / 256;
+  const int64_t cap = int64_t(g_num_sms > 0 ? g_num_sms : 148) * 16;
+  if (blocks > cap) blocks = cap;
+  return status_from(launch_pdl(tf32_lo_kernel, dim3(unsigned(blocks)), dim3(256), 0, q, true,
+                                src, lds, dst, ldd, rows, cols / 4, batch, sstride, dstride));
 }
 
 int* device_status_ptr() {

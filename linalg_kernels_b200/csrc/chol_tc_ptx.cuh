@@ -152,6 +152,7 @@ __device__ __forceinline__ void split4(float4* hi_p, float4* lo_p) {
 // Origin of the view inside the tensor maps (element coordinates: x = column, y = row).
 struct TmaOrigin {
   int px, py, qx, qy;
+  int lpx, lqx;  // K origin of P and Q inside precomputed-lo buffers (rows as for P and Q)
 };
 
 // Split of chunk i of a 128B-swizzled K-major tile (8 chunks of 4 floats per row; the

@@ -208,4 +208,14 @@ def test_fused_panel_step_option(name):
     try:
         _check_full_config(name, batch=8)
     finally:
-        lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, 0)
+        lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, -1)
+
+
+def test_three_launch_step_at_large_n():
+    """n = 16384 through the three-launch step (the default there is the fused step)."""
+    lib = _lib.load()
+    lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, 0)
+    try:
+        _check_full_config("b1n16384")
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, -1)

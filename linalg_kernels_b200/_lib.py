@@ -28,6 +28,8 @@ CHOL_ERR_SCRATCH_LIMIT = 8
 CHOL_OPT_GEMM_ENGINE = 1
 CHOL_OPT_FUSED_PANEL = 2
 CHOL_OPT_OUTER_WIDTH = 3
+CHOL_OPT_LOOKAHEAD = 4
+CHOL_OPT_CHAIN_SMS = 5
 ENGINE_AUTO, ENGINE_FMA, ENGINE_TENSOR = 0, 1, 2
 
 _i64 = ctypes.c_int64

@@ -110,11 +110,41 @@ struct BlockedMaps {
 };
 
 int gemm_on(const GemmArgs& g, const BlockedMaps& bm, const TcMatrixMaps& pm,
-            const TcMatrixMaps& qm, cudaStream_t q) {
+            const TcMatrixMaps& qm, cudaStream_t q, int max_ctas = 0) {
   if (g.m <= 0 || g.ncols <= 0) return CHOL_OK;
-  if (bm.ok && g_gemm_engine != 1) return launch_gemm_tc_mapped(g, pm, qm, q, true);
+  if (bm.ok && g_gemm_engine != 1) return launch_gemm_tc_mapped(g, pm, qm, q, true, max_ctas);
   if (g_gemm_engine == 2) return CHOL_ERR_UNSUPPORTED;
   return launch_gemm_simt(g, q, true);
+}
+
+// Look-ahead between outer panels (large n): the trailing update of panel J is split into
+// T1 (panel J+1's own columns, on the caller's queue) and T2 (everything to its right, on a
+// library side queue with its grid capped so that kChainSms SMs stay free); panel J+1's
+// chain of small kernels then runs beside T2.
+int g_lookahead = 0;
+int g_chain_sms = 24;
+
+struct SideQueue {
+  std::once_flag once;
+  std::mutex order;  // one enqueue at a time: the events are shared by all callers
+  bool ok = false;
+  cudaStream_t s = nullptr;
+  cudaEvent_t ready[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+};
+
+SideQueue* side_queue(int dev) {
+  static SideQueue qs[64];
+  if (dev < 0 || dev >= 64) return nullptr;
+  SideQueue* sq = &qs[dev];
+  std::call_once(sq->once, [sq]() {
+    bool ok = cudaStreamCreateWithFlags(&sq->s, cudaStreamNonBlocking) == cudaSuccess;
+    for (int i = 0; i < 2 && ok; ++i)
+      ok = cudaEventCreateWithFlags(&sq->ready[i], cudaEventDisableTiming) == cudaSuccess &&
+           cudaEventCreateWithFlags(&sq->done[i], cudaEventDisableTiming) == cudaSuccess;
+    sq->ok = ok;
+  });
+  return sq->ok ? sq : nullptr;
 }
 
 int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, float* Tws,
@@ -136,6 +166,12 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
             panel_make_map(pmap, L, n, batch);
   if (!bm.ok || (lo && !tc_make_matrix_maps(lo, n, NBw, NBw, batch, n * NBw, &lomap)))
     lo = nullptr;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  SideQueue* sq = (lo != nullptr && g_lookahead) ? side_queue(dev) : nullptr;
+  std::unique_lock<std::mutex> hold;
+  if (sq != nullptr) hold = std::unique_lock<std::mutex>(sq->order);
+  int pending = -1, ev = 0, chain_cap = 0;
   const bool fused = bm.ok && use_fused(batch, n);
   if (fused && cudaMemsetAsync(counters, 0, size_t(batch) * sizeof(unsigned), q) != cudaSuccess)
     return CHOL_ERR_LAUNCH;
@@ -173,7 +209,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
         u.diag_offset = 0;
         u.lower_only = 1;
         u.batch = batch;
-        st = gemm_on(u, bm, bm.L, bm.L, q);
+        st = gemm_on(u, bm, bm.L, bm.L, q, chain_cap);
         if (st) return st;
       }
       st = launch_potrf_block(L, mstride, n, L, mstride, n, batch, k, kb, Tws, info, q, true);
@@ -198,7 +234,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       s.beta = 0.f;
       s.lower_only = 0;
       s.batch = batch;
-      st = gemm_on(s, bm, bm.L, bm.T, q);
+      st = gemm_on(s, bm, bm.L, bm.T, q, chain_cap);
       if (st) return st;
     }
     const int64_t rest = n - K0 - KB;
@@ -222,10 +258,43 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       t.lower_only = 1;
       t.batch = batch;
       if (lo != nullptr && KB == NBw && g_gemm_engine != 1) {
+        // the previous T2 must finish before the lo buffer and its columns are reused
+        if (pending >= 0) {
+          if (cudaStreamWaitEvent(q, sq->done[pending], 0) != cudaSuccess) return CHOL_ERR_LAUNCH;
+          pending = -1;
+        }
         // low parts of the panel rows below it, computed once, read by every tile
         st = launch_tf32_lo(L + (K0 + KB) * n + K0, n, lo + (K0 + KB) * NBw, NBw, rest, KB, batch,
                             mstride, n * NBw, q);
         if (st) return st;
+        const int64_t K0n = K0 + KB;
+        const int64_t KBn = rest < NBw ? rest : NBw;
+        if (sq != nullptr && rest > KBn) {
+          // T1: next panel's columns, here; T2: the rest, on the side queue
+          GemmArgs t1 = t;
+          t1.ncols = KBn;
+          st = launch_gemm_tc_mapped_lo(t1, bm.L, bm.L, lomap, 0, q, true);
+          if (st) return st;
+          if (cudaEventRecord(sq->ready[ev], q) != cudaSuccess ||
+              cudaStreamWaitEvent(sq->s, sq->ready[ev], 0) != cudaSuccess)
+            return CHOL_ERR_LAUNCH;
+          GemmArgs t2 = t;
+          t2.C = L + (K0n + KBn) * n + (K0n + KBn);
+          t2.P = L + (K0n + KBn) * n + K0;
+          t2.Q = t2.P;
+          t2.m = rest - KBn;
+          t2.ncols = rest - KBn;
+          int sms = 148;
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+          st = launch_gemm_tc_mapped_lo(t2, bm.L, bm.L, lomap, 0, sq->s, false, sms - g_chain_sms);
+          if (st) return st;
+          if (cudaEventRecord(sq->done[ev], sq->s) != cudaSuccess) return CHOL_ERR_LAUNCH;
+          pending = ev;
+          ev ^= 1;
+          chain_cap = g_chain_sms;
+          continue;
+        }
+        chain_cap = 0;
         st = launch_gemm_tc_mapped_lo(t, bm.L, bm.L, lomap, 0, q, true);
       } else {
         st = gemm_on(t, bm, bm.L, bm.L, q);
@@ -233,6 +302,8 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       if (st) return st;
     }
   }
+  if (pending >= 0 && cudaStreamWaitEvent(q, sq->done[pending], 0) != cudaSuccess)
+    return CHOL_ERR_LAUNCH;
   return CHOL_OK;
 }
 
@@ -252,7 +323,12 @@ int64_t blocked_launches(int64_t n, bool fused) {
       count += 1;              // diagonal block
       if (n - k - kb > 0) count += 1;  // panel solve
     }
-    if (n - K0 - KB > 0) count += (n % 4 == 0 && NB < n) ? 2 : 1;  // (+ lo pass)
+    const int64_t rest = n - K0 - KB;
+    if (rest > 0) {
+      const bool pre = n % 4 == 0 && NB < n;
+      count += pre ? 2 : 1;                          // (lo pass +) trailing update
+      if (pre && g_lookahead && rest > NB) count += 1;  // split into T1 + T2
+    }
   }
   return count;
 }
@@ -402,6 +478,16 @@ int chol_set_option(int option, int value) {
   if (option == CHOL_OPT_OUTER_WIDTH) {
     if (value < 0 || value % 64) return CHOL_ERR_INVALID_ARG;
     g_outer_width = value;
+    return CHOL_OK;
+  }
+  if (option == CHOL_OPT_LOOKAHEAD) {
+    if (value < 0 || value > 1) return CHOL_ERR_INVALID_ARG;
+    g_lookahead = value;
+    return CHOL_OK;
+  }
+  if (option == CHOL_OPT_CHAIN_SMS) {
+    if (value < 1 || value > 120) return CHOL_ERR_INVALID_ARG;
+    g_chain_sms = value;
     return CHOL_OK;
   }
   if (option == CHOL_OPT_FUSED_PANEL) {

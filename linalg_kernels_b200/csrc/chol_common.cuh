@@ -84,16 +84,8 @@ __device__ __forceinline__ uint64_t pack2(float x, float y) {
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
   return r;
 }
-__device__ __forceinline__ float lo_of(uint64_t v) {
-  float x, y;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v));
-  return x;
-}
-__device__ __forceinline__ float hi_of(uint64_t v) {
-  float x, y;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v));
-  return y;
-}
+__device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float(uint32_t(v)); }
+__device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
 
 // Host-side launch helper: cudaLaunchKernelEx with the PDL attribute.
 template <typename... KArgs, typename... Args>
@@ -170,10 +162,12 @@ struct TcMatrixMaps {
 };
 bool tc_make_matrix_maps(const float* base, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
                          int64_t bstride, TcMatrixMaps* maps);
+// max_ctas > 0 caps the persistent grid (leaves SMs for concurrent work on another queue).
 int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
-                          cudaStream_t q, bool pdl);
+                          cudaStream_t q, bool pdl, int max_ctas = 0);
 int launch_gemm_tc_mapped_lo(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
-                             const TcMatrixMaps& lm, int64_t lk, cudaStream_t q, bool pdl);
+                             const TcMatrixMaps& lm, int64_t lk, cudaStream_t q, bool pdl,
+                             int max_ctas = 0);
 int launch_tf32_lo(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows,
                    int64_t cols, int64_t batch, int64_t sstride, int64_t dstride, cudaStream_t q);
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status);

@@ -457,7 +457,8 @@ int g_num_sms = 0;
 template <int BN>
 int launch_tc_maps(const GemmArgs& g, const CUtensorMap& mp, const CUtensorMap& mq,
                    TmaOrigin org, cudaStream_t q, bool pdl, int* status,
-                   const CUtensorMap* mplo = nullptr, const CUtensorMap* mqlo = nullptr) {
+                   const CUtensorMap* mplo = nullptr, const CUtensorMap* mqlo = nullptr,
+                   int max_ctas = 0) {
   using Cfg = TcCfg<BN>;
   const TileSpace ts = make_tiles(g, BN);
   if (ts.total == 0) return CHOL_OK;
@@ -467,7 +468,8 @@ int launch_tc_maps(const GemmArgs& g, const CUtensorMap& mp, const CUtensorMap& 
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  const int64_t ctas = ts.total < sms ? ts.total : sms;
+  int64_t ctas = ts.total < sms ? ts.total : sms;
+  if (max_ctas > 0 && ctas > max_ctas) ctas = max_ctas;
   if (mplo != nullptr && mqlo != nullptr)
     return status_from(launch_pdl(tc_gemm_kernel<BN, true>, dim3(unsigned(ctas)), dim3(kThreads),
                                   Cfg::SMEM, q, pdl, mp, mq, *mplo, *mqlo, g, ts, org, status));
@@ -520,7 +522,7 @@ bool tc_make_matrix_maps(const float* base, int64_t rows, int64_t cols, int64_t 
 
 // P and Q are views of the matrices behind pm / qm (element offsets from their bases).
 int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
-                          cudaStream_t q, bool pdl) {
+                          cudaStream_t q, bool pdl, int max_ctas) {
   const int64_t po = g.P - pm.base, qo = g.Q - qm.base;
   if (po < 0 || qo < 0 || g.ldp != pm.ld || g.ldq != qm.ld) return CHOL_ERR_INVALID_ARG;
   if (g.batch > 1 && (g.pstride != pm.bstride || g.qstride != qm.bstride))
@@ -530,18 +532,19 @@ int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMat
   const CUtensorMap& mp = *reinterpret_cast<const CUtensorMap*>(pm.p128);
   if (g.ncols <= 64)
     return launch_tc_maps<64>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q64), org, q, pdl,
-                              nullptr);
+                              nullptr, nullptr, nullptr, max_ctas);
   if (g.ncols <= 128)
     return launch_tc_maps<128>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q128), org, q,
-                               pdl, nullptr);
+                               pdl, nullptr, nullptr, nullptr, max_ctas);
   return launch_tc_maps<256>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q256), org, q, pdl,
-                             nullptr);
+                             nullptr, nullptr, nullptr, max_ctas);
 }
 
 // As launch_gemm_tc_mapped with the low parts of P and Q read from a precomputed buffer
 // (maps lm, rows indexed like P/Q's matrix, K origin lk) instead of split in the kernel.
 int launch_gemm_tc_mapped_lo(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
-                             const TcMatrixMaps& lm, int64_t lk, cudaStream_t q, bool pdl) {
+                             const TcMatrixMaps& lm, int64_t lk, cudaStream_t q, bool pdl,
+                             int max_ctas) {
   const int64_t po = g.P - pm.base, qo = g.Q - qm.base;
   if (po < 0 || qo < 0 || g.ldp != pm.ld || g.ldq != qm.ld) return CHOL_ERR_INVALID_ARG;
   TmaOrigin org{int(po % pm.ld), int(po / pm.ld), int(qo % qm.ld), int(qo / qm.ld), int(lk),
@@ -551,12 +554,15 @@ int launch_gemm_tc_mapped_lo(const GemmArgs& g, const TcMatrixMaps& pm, const Tc
   const CUtensorMap& mpl = *reinterpret_cast<const CUtensorMap*>(lm.p128);
   if (g.ncols <= 64)
     return launch_tc_maps<64>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q64), org, q, pdl,
-                              nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q64));
+                              nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q64),
+                              max_ctas);
   if (g.ncols <= 128)
     return launch_tc_maps<128>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q128), org, q,
-                               pdl, nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q128));
+                               pdl, nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q128),
+                               max_ctas);
   return launch_tc_maps<256>(g, mp, *reinterpret_cast<const CUtensorMap*>(qm.q256), org, q, pdl,
-                             nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q256));
+                             nullptr, &mpl, reinterpret_cast<const CUtensorMap*>(lm.q256),
+                             max_ctas);
 }
 
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {

@@ -82,10 +82,12 @@ bool overlaps_partially(const float* a, const float* b, int64_t count) {
 }
 
 // Workspace of the blocked path: the inverse diagonal blocks (64 x 64 floats per matrix,
-// used by the FP32-FMA schedule and the building blocks), one arrival counter per matrix
-// for the fused panel step, and (when there is a trailing update, n > outer width) the
-// low TF32 parts of one outer panel (n x NB floats per matrix) so that the trailing GEMM
-// loads them instead of splitting in shared memory. Only the first two are required.
+// used by the FP32-FMA schedule and the building blocks) and one arrival counter per matrix
+// for the fused panel step are required. When there is a trailing update (n > outer width
+// NB, n % 4 == 0) two optional regions follow: the panel buffer (n x NB floats per matrix),
+// which holds the panel solve's output and then the low TF32 parts of the solved panel that
+// the trailing GEMM loads instead of splitting in shared memory, and V = inv(L11) of the
+// panel's NB x NB diagonal block (NB x NB floats per matrix).
 size_t blocked_workspace_min(int64_t batch, int64_t n) {
   if (n <= 64) return 0;
   const size_t tinv = size_t(batch) * kBlock * kBlock * sizeof(float);
@@ -97,8 +99,18 @@ size_t blocked_lo_bytes(int64_t batch, int64_t n) {
   if (n <= 64 || NB >= n || n % 4) return 0;
   return size_t(batch) * size_t(n) * size_t(NB) * sizeof(float);
 }
+// V, then the diagonal-block kernel's flags (kDiagFlags ints per matrix) and one ticket
+// counter per outer panel; all zeroed once per call.
+size_t blocked_inv_bytes(int64_t batch, int64_t n) {
+  const int64_t NB = outer_width(n);
+  if (blocked_lo_bytes(batch, n) == 0 || NB % kBlock || NB > 16 * kBlock) return 0;
+  const int64_t panels = (n + NB - 1) / NB;
+  return size_t(batch) * size_t(NB) * size_t(NB) * sizeof(float) +
+         size_t(batch) * kDiagFlags * sizeof(int) + ((size_t(panels) * 4 + 255) & ~size_t(255));
+}
 size_t blocked_workspace(int64_t batch, int64_t n) {
-  return blocked_workspace_min(batch, n) + blocked_lo_bytes(batch, n);
+  return blocked_workspace_min(batch, n) + blocked_lo_bytes(batch, n) +
+         blocked_inv_bytes(batch, n);
 }
 
 // Tensor-core GEMMs of one call share tensor maps built once over L and the inverse blocks;
@@ -147,17 +159,30 @@ SideQueue* side_queue(int dev) {
   return sq->ok ? sq : nullptr;
 }
 
+// Panel solve by the inverse of the diagonal block (default; needs the optional workspace):
+// one launch (diag_block_kernel) factors the panel's NB x NB diagonal block and writes
+// V = inv(L11), and the rows below the block are solved by ONE tensor-core GEMM,
+// X = A21 V^T, over every row at once. 2 = the same, with the block factored by the chain
+// of small kernels and V from trtri_panel. 0 = the chain covers every row of the panel
+// (left-looking GEMMs with m = n - k).
+int g_panel_inverse = 1;
+
 int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, float* Tws,
                 size_t ws_bytes, cudaStream_t q) {
   unsigned int* counters = reinterpret_cast<unsigned int*>(Tws + batch * kBlock * kBlock);
   const int64_t mstride = n * n;
+  const size_t min_bytes = blocked_workspace_min(batch, n);
   const size_t lo_bytes = blocked_lo_bytes(batch, n);
-  float* lo = (lo_bytes && ws_bytes >= blocked_workspace_min(batch, n) + lo_bytes)
-                  ? reinterpret_cast<float*>(reinterpret_cast<char*>(Tws) +
-                                             blocked_workspace_min(batch, n))
+  const size_t inv_bytes = blocked_inv_bytes(batch, n);
+  char* ws = reinterpret_cast<char*>(Tws);
+  float* lo = (lo_bytes && ws_bytes >= min_bytes + lo_bytes)
+                  ? reinterpret_cast<float*>(ws + min_bytes)
                   : nullptr;
+  float* V = (lo && inv_bytes && ws_bytes >= min_bytes + lo_bytes + inv_bytes)
+                 ? reinterpret_cast<float*>(ws + min_bytes + lo_bytes)
+                 : nullptr;
   BlockedMaps bm;
-  TcMatrixMaps lomap;
+  TcMatrixMaps lomap, vmap;
   alignas(64) unsigned char pmap[128];
   const int64_t NBw = outer_width(n);
   if (g_gemm_engine != 1)
@@ -166,6 +191,14 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
             panel_make_map(pmap, L, n, batch);
   if (!bm.ok || (lo && !tc_make_matrix_maps(lo, n, NBw, NBw, batch, n * NBw, &lomap)))
     lo = nullptr;
+  if (!lo || !g_panel_inverse || (V && !tc_make_matrix_maps(V, NBw, NBw, NBw, batch, NBw * NBw,
+                                                             &vmap)))
+    V = nullptr;
+  const bool inv = V != nullptr;
+  const bool diag_kernel = inv && g_panel_inverse == 1;
+  int* dflags = inv ? reinterpret_cast<int*>(V + batch * NBw * NBw) : nullptr;
+  unsigned* tickets = inv ? reinterpret_cast<unsigned*>(dflags + batch * kDiagFlags) : nullptr;
+  if (inv && cudaMemsetAsync(V, 0, inv_bytes, q) != cudaSuccess) return CHOL_ERR_LAUNCH;
   int dev = 0;
   cudaGetDevice(&dev);
   SideQueue* sq = (lo != nullptr && g_lookahead) ? side_queue(dev) : nullptr;
@@ -177,14 +210,36 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
     return CHOL_ERR_LAUNCH;
   int st = launch_copy_lower(A, L, batch, n, q, true);
   if (st) return st;
-  const int64_t NB = outer_width(n);
+  // the previous panel's side-queue update must finish before the panel buffer is rewritten
+  auto join_pending = [&]() -> int {
+    if (pending < 0) return CHOL_OK;
+    if (cudaStreamWaitEvent(q, sq->done[pending], 0) != cudaSuccess) return CHOL_ERR_LAUNCH;
+    pending = -1;
+    return CHOL_OK;
+  };
+  const int64_t NB = NBw;
   for (int64_t K0 = 0; K0 < n; K0 += NB) {
     const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
-    for (int64_t k = K0; k < K0 + KB; k += kBlock) {
+    const int64_t rest = n - K0 - KB;
+    // rows the in-panel chain updates and solves: the diagonal block only, or every row
+    const int64_t chain_end = inv ? K0 + KB : n;
+    const bool one_launch = diag_kernel && KB % kBlock == 0;
+    if (one_launch) {
+      st = launch_diag_block(L + K0 * n + K0, mstride, n, V, NBw * NBw, NBw, int(KB / kBlock),
+                             rest > 0, dflags, tickets + K0 / NB, int(K0 / NB) + 1, info, K0,
+                             batch, q);
+      if (st) return st;
+    }
+    for (int64_t k = K0; !one_launch && k < K0 + KB; k += kBlock) {
       const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
+      // inv(L_kk) goes to V's diagonal block (inverse schedule) or the 64 x 64 slot
+      float* Tk = inv ? V + (k - K0) * NBw + (k - K0) : Tws;
+      const int64_t tstride = inv ? NBw * NBw : kBlock * kBlock;
+      const int64_t tld = inv ? NBw : kBlock;
       if (fused) {
         // one fused launch: left-looking update, diagonal factor + inverse, panel solve
-        st = launch_panel_step(pmap, L, n, batch, k, kb, K0, info, counters, q);
+        st = launch_panel_step(pmap, L, n, batch, k, kb, K0, info, counters, q, chain_end,
+                               inv ? Tk : nullptr, tstride, tld);
         if (st) return st;
         continue;
       }
@@ -201,7 +256,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
         u.Q = u.P;
         u.qstride = mstride;
         u.ldq = n;
-        u.m = n - k;
+        u.m = chain_end - k;
         u.ncols = kb;
         u.K = k - K0;
         u.alpha = -1.f;
@@ -212,9 +267,10 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
         st = gemm_on(u, bm, bm.L, bm.L, q, chain_cap);
         if (st) return st;
       }
-      st = launch_potrf_block(L, mstride, n, L, mstride, n, batch, k, kb, Tws, info, q, true);
+      st = launch_potrf_block(L, mstride, n, L, mstride, n, batch, k, kb, Tk, info, q, true,
+                              tstride, tld);
       if (st) return st;
-      const int64_t below = n - k - kb;
+      const int64_t below = chain_end - k - kb;
       if (below <= 0) continue;
       // panel solve: L[k+kb:, k:k+kb] <- L[k+kb:, k:k+kb] * T^T (in place)
       GemmArgs s{};
@@ -224,9 +280,9 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       s.P = s.C;
       s.pstride = mstride;
       s.ldp = n;
-      s.Q = Tws;
-      s.qstride = kBlock * kBlock;
-      s.ldq = kBlock;
+      s.Q = Tk;
+      s.qstride = tstride;
+      s.ldq = tld;
       s.m = below;
       s.ncols = kb;
       s.K = kb;
@@ -234,101 +290,135 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       s.beta = 0.f;
       s.lower_only = 0;
       s.batch = batch;
-      st = gemm_on(s, bm, bm.L, bm.T, q, chain_cap);
+      st = gemm_on(s, bm, bm.L, inv ? vmap : bm.T, q, chain_cap);
       if (st) return st;
     }
-    const int64_t rest = n - K0 - KB;
-    if (rest > 0) {
-      GemmArgs t{};
-      t.C = L + (K0 + KB) * n + (K0 + KB);
-      t.cstride = mstride;
-      t.ldc = n;
-      t.P = L + (K0 + KB) * n + K0;
-      t.pstride = mstride;
-      t.ldp = n;
-      t.Q = t.P;
-      t.qstride = mstride;
-      t.ldq = n;
-      t.m = rest;
-      t.ncols = rest;
-      t.K = KB;
-      t.alpha = -1.f;
-      t.beta = 1.f;
-      t.diag_offset = 0;
-      t.lower_only = 1;
-      t.batch = batch;
-      if (lo != nullptr && KB == NBw && g_gemm_engine != 1) {
-        // the previous T2 must finish before the lo buffer and its columns are reused
-        if (pending >= 0) {
-          if (cudaStreamWaitEvent(q, sq->done[pending], 0) != cudaSuccess) return CHOL_ERR_LAUNCH;
-          pending = -1;
-        }
-        // low parts of the panel rows below it, computed once, read by every tile
-        st = launch_tf32_lo(L + (K0 + KB) * n + K0, n, lo + (K0 + KB) * NBw, NBw, rest, KB, batch,
-                            mstride, n * NBw, q);
+    if (rest <= 0) continue;
+    GemmArgs t{};
+    t.C = L + (K0 + KB) * n + (K0 + KB);
+    t.cstride = mstride;
+    t.ldc = n;
+    t.P = L + (K0 + KB) * n + K0;
+    t.pstride = mstride;
+    t.ldp = n;
+    t.Q = t.P;
+    t.qstride = mstride;
+    t.ldq = n;
+    t.m = rest;
+    t.ncols = rest;
+    t.K = KB;
+    t.alpha = -1.f;
+    t.beta = 1.f;
+    t.diag_offset = 0;
+    t.lower_only = 1;
+    t.batch = batch;
+    if (lo == nullptr || KB != NBw || g_gemm_engine == 1) {
+      st = gemm_on(t, bm, bm.L, bm.L, q);
+      if (st) return st;
+      continue;
+    }
+    if ((st = join_pending())) return st;
+    float* pbuf = lo + (K0 + KB) * NBw;  // panel buffer rows of the rows below the block
+    if (inv) {
+      if (!one_launch) {
+        st = launch_trtri_panel(L + K0 * n + K0, mstride, n, V, NBw * NBw, NBw,
+                                int(KB / kBlock), batch, q);
         if (st) return st;
-        const int64_t K0n = K0 + KB;
-        const int64_t KBn = rest < NBw ? rest : NBw;
-        if (sq != nullptr && rest > KBn) {
-          // T1: next panel's columns, here; T2: the rest, on the side queue
-          GemmArgs t1 = t;
-          t1.ncols = KBn;
-          st = launch_gemm_tc_mapped_lo(t1, bm.L, bm.L, lomap, 0, q, true);
-          if (st) return st;
-          if (cudaEventRecord(sq->ready[ev], q) != cudaSuccess ||
-              cudaStreamWaitEvent(sq->s, sq->ready[ev], 0) != cudaSuccess)
-            return CHOL_ERR_LAUNCH;
-          GemmArgs t2 = t;
-          t2.C = L + (K0n + KBn) * n + (K0n + KBn);
-          t2.P = L + (K0n + KBn) * n + K0;
-          t2.Q = t2.P;
-          t2.m = rest - KBn;
-          t2.ncols = rest - KBn;
-          int sms = 148;
-          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-          st = launch_gemm_tc_mapped_lo(t2, bm.L, bm.L, lomap, 0, sq->s, false, sms - g_chain_sms);
-          if (st) return st;
-          if (cudaEventRecord(sq->done[ev], sq->s) != cudaSuccess) return CHOL_ERR_LAUNCH;
-          pending = ev;
-          ev ^= 1;
-          chain_cap = g_chain_sms;
-          continue;
-        }
-        chain_cap = 0;
-        st = launch_gemm_tc_mapped_lo(t, bm.L, bm.L, lomap, 0, q, true);
-      } else {
-        st = gemm_on(t, bm, bm.L, bm.L, q);
       }
+      // X = A21 V^T for every row below the diagonal block, into the panel buffer (the GEMM
+      // reads whole rows of A21, so it cannot write them in place)
+      GemmArgs x{};
+      x.C = pbuf;
+      x.cstride = n * NBw;
+      x.ldc = NBw;
+      x.P = t.P;
+      x.pstride = mstride;
+      x.ldp = n;
+      x.Q = V;
+      x.qstride = NBw * NBw;
+      x.ldq = NBw;
+      x.m = rest;
+      x.ncols = KB;
+      x.K = KB;
+      x.alpha = 1.f;
+      x.beta = 0.f;
+      x.lower_only = 0;
+      x.batch = batch;
+      st = launch_gemm_tc_mapped(x, bm.L, vmap, q, true);
       if (st) return st;
+      // L21 <- X, and the panel buffer <- low TF32 parts of X for the trailing GEMM
+      st = launch_tf32_lo(pbuf, NBw, pbuf, NBw, rest, KB, batch, n * NBw, n * NBw, q,
+                          L + (K0 + KB) * n + K0, n, mstride);
+    } else {
+      // low parts of the panel rows below it, computed once, read by every tile
+      st = launch_tf32_lo(t.P, n, pbuf, NBw, rest, KB, batch, mstride, n * NBw, q);
     }
+    if (st) return st;
+    const int64_t K0n = K0 + KB;
+    const int64_t KBn = rest < NBw ? rest : NBw;
+    if (sq != nullptr && rest > KBn) {
+      // T1: next panel's columns, here; T2: the rest, on the side queue
+      GemmArgs t1 = t;
+      t1.ncols = KBn;
+      st = launch_gemm_tc_mapped_lo(t1, bm.L, bm.L, lomap, 0, q, true);
+      if (st) return st;
+      if (cudaEventRecord(sq->ready[ev], q) != cudaSuccess ||
+          cudaStreamWaitEvent(sq->s, sq->ready[ev], 0) != cudaSuccess)
+        return CHOL_ERR_LAUNCH;
+      GemmArgs t2 = t;
+      t2.C = L + (K0n + KBn) * n + (K0n + KBn);
+      t2.P = L + (K0n + KBn) * n + K0;
+      t2.Q = t2.P;
+      t2.m = rest - KBn;
+      t2.ncols = rest - KBn;
+      int sms = 148;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      st = launch_gemm_tc_mapped_lo(t2, bm.L, bm.L, lomap, 0, sq->s, false, sms - g_chain_sms);
+      if (st) return st;
+      if (cudaEventRecord(sq->done[ev], sq->s) != cudaSuccess) return CHOL_ERR_LAUNCH;
+      pending = ev;
+      ev ^= 1;
+      chain_cap = inv ? 0 : g_chain_sms;
+      continue;
+    }
+    chain_cap = 0;
+    st = launch_gemm_tc_mapped_lo(t, bm.L, bm.L, lomap, 0, q, true);
+    if (st) return st;
   }
-  if (pending >= 0 && cudaStreamWaitEvent(q, sq->done[pending], 0) != cudaSuccess)
-    return CHOL_ERR_LAUNCH;
-  return CHOL_OK;
+  return join_pending();
 }
 
 // Launch count of run_blocked for (batch, n); keep in step with the schedule above.
-int64_t blocked_launches(int64_t n, bool fused) {
+int64_t blocked_launches(int64_t batch, int64_t n, bool fused) {
+  const bool pre = blocked_lo_bytes(batch, n) > 0 && g_gemm_engine != 1;
+  const bool inv = pre && g_panel_inverse && blocked_inv_bytes(batch, n) > 0;
+  const bool diag_kernel = inv && g_panel_inverse == 1;
   int64_t count = 1;  // copy_lower
   const int64_t NB = outer_width(n);
   for (int64_t K0 = 0; K0 < n; K0 += NB) {
     const int64_t KB = (n - K0) < NB ? (n - K0) : NB;
-    for (int64_t k = K0; k < K0 + KB; k += kBlock) {
+    const int64_t rest = n - K0 - KB;
+    const int64_t chain_end = inv ? K0 + KB : n;
+    const bool one_launch = diag_kernel && KB % kBlock == 0;
+    if (one_launch) count += 1;  // diagonal block + its inverse
+    for (int64_t k = K0; !one_launch && k < K0 + KB; k += kBlock) {
       const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
       if (fused) {
         count += 1;
         continue;
       }
-      if (k > K0) count += 1;  // left-looking panel update
-      count += 1;              // diagonal block
-      if (n - k - kb > 0) count += 1;  // panel solve
+      if (k > K0) count += 1;                  // left-looking panel update
+      count += 1;                              // diagonal block
+      if (chain_end - k - kb > 0) count += 1;  // panel solve
     }
-    const int64_t rest = n - K0 - KB;
-    if (rest > 0) {
-      const bool pre = n % 4 == 0 && NB < n;
-      count += pre ? 2 : 1;                          // (lo pass +) trailing update
-      if (pre && g_lookahead && rest > NB) count += 1;  // split into T1 + T2
+    if (rest <= 0) continue;
+    if (!pre) {
+      count += 1;  // trailing update
+      continue;
     }
+    count += inv ? (one_launch ? 2 : 3) : 1;     // ((trtri +) solve GEMM +) split/lo pass
+    count += 1;                                  // trailing update
+    if (g_lookahead && rest > NB) count += 1;    // split into T1 + T2
   }
   return count;
 }
@@ -365,8 +455,10 @@ int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int
 }
 
 int prepare_kernels(int /*device*/) {
-  return (prepare_tc() == cudaSuccess && prepare_panel() == cudaSuccess) ? CHOL_OK
-                                                                          : CHOL_ERR_DEVICE;
+  return (prepare_tc() == cudaSuccess && prepare_panel() == cudaSuccess &&
+          prepare_blocked() == cudaSuccess)
+             ? CHOL_OK
+             : CHOL_ERR_DEVICE;
 }
 
 int g_gemm_engine = 0;
@@ -466,7 +558,7 @@ int64_t chol_launch_count(int64_t batch, int64_t n) {
   if (n <= 64) return 1;
   // the fused panel step runs when the tensor-core engine is allowed and rows are
   // 16-byte multiples (the usual case: n % 4 == 0)
-  return blocked_launches(n, use_fused(batch, n) && g_gemm_engine != 1 && n % 4 == 0);
+  return blocked_launches(batch, n, use_fused(batch, n) && g_gemm_engine != 1 && n % 4 == 0);
 }
 
 int chol_set_option(int option, int value) {
@@ -488,6 +580,11 @@ int chol_set_option(int option, int value) {
   if (option == CHOL_OPT_CHAIN_SMS) {
     if (value < 1 || value > 120) return CHOL_ERR_INVALID_ARG;
     g_chain_sms = value;
+    return CHOL_OK;
+  }
+  if (option == CHOL_OPT_PANEL_INVERSE) {
+    if (value < 0 || value > 2) return CHOL_ERR_INVALID_ARG;
+    g_panel_inverse = value;
     return CHOL_OK;
   }
   if (option == CHOL_OPT_FUSED_PANEL) {

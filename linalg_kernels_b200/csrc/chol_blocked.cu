@@ -70,8 +70,8 @@ int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaSt
 //   S (+ m*sstride) with leading dimension lds is where the block is read from (A for the
 //   first block when the copy is fused, else L); the factor goes to L (+ m*stride, ld).
 //   Strict upper part of the block is written as zeros.
-//   Tinv (+ m*4096), if not null, receives inv(L_kk) as a row-major 64 x 64 lower
-//   triangle (rows/cols >= kb are identity).
+//   Tinv (+ m*tstride, leading dimension tld), if not null, receives inv(L_kk) as a 64 x 64
+//   lower triangle with explicit zeros above the diagonal (rows/cols >= kb are identity).
 //   info[m]: first failing global column (1-based); written when info[m] == 0 or k == 0.
 // =====================================================================================
 constexpr int kPB = 64;         // block size handled by one CTA
@@ -80,7 +80,8 @@ constexpr int kPBLD = kPB + 4;  // smem row stride
 __global__ void __launch_bounds__(128)
     potrf_block_kernel(const float* __restrict__ S, int64_t sstride, int64_t lds,
                        float* __restrict__ L, int64_t stride, int64_t ld, int64_t k, int kb,
-                       float* __restrict__ Tinv, int* __restrict__ info) {
+                       float* __restrict__ Tinv, int64_t tstride, int64_t tld,
+                       int* __restrict__ info) {
   __shared__ __align__(16) float tile[kPB * kPBLD];
   __shared__ __align__(16) float col[2 * kPB];
   __shared__ float rdiag[kPB];
@@ -109,44 +110,7 @@ __global__ void __launch_bounds__(128)
   __syncthreads();
 
   if (tid < 32) {
-    uint64_t a[2][32];
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      const float* rp = tile + (s * 32 + tid) * kPBLD;
-#pragma unroll
-      for (int q = 0; q < (s + 1) * 8; ++q) {
-        const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(rp + 4 * q);
-        a[s][2 * q] = v.x;
-        a[s][2 * q + 1] = v.y;
-      }
-    }
-    warp_potrf_rows<64>(a, col, tid);
-    __syncwarp();
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      const int i = s * 32 + tid;
-      float* rp = tile + i * kPBLD;
-#pragma unroll
-      for (int q = 0; q < kPB / 4; ++q) {
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (4 * q < (s + 1) * 32) {
-          v.x = (4 * q + 0 <= i) ? lo_of(a[s][2 * q]) : 0.f;
-          v.y = (4 * q + 1 <= i) ? hi_of(a[s][2 * q]) : 0.f;
-          v.z = (4 * q + 2 <= i) ? lo_of(a[s][2 * q + 1]) : 0.f;
-          v.w = (4 * q + 3 <= i) ? hi_of(a[s][2 * q + 1]) : 0.f;
-        }
-        *reinterpret_cast<float4*>(rp + 4 * q) = v;
-      }
-    }
-    __syncwarp();
-    const float d0 = tile[tid * kPBLD + tid];
-    const float d1 = tile[(tid + 32) * kPBLD + tid + 32];
-    rdiag[tid] = __frcp_rn(d0);
-    rdiag[tid + 32] = __frcp_rn(d1);
-    // first row whose diagonal is not > 0 (NaN included) is the first failing column
-    const unsigned b0 = __ballot_sync(0xffffffffu, !(d0 > 0.f));
-    const unsigned b1 = __ballot_sync(0xffffffffu, !(d1 > 0.f));
-    const int fail = b0 ? __ffs(b0) : (b1 ? 32 + __ffs(b1) : 0);
+    const int fail = tile64_potrf<kPBLD>(tile, col, rdiag, tid);
     if (tid == 0 && info != nullptr) {
       const int f = (fail > kb) ? 0 : fail;
       if (k == 0)
@@ -164,40 +128,157 @@ __global__ void __launch_bounds__(128)
       dst[r * ld + c] = tile[r * kPBLD + c];
     }
   } else if (Tinv != nullptr) {
-    // threads 0..63: column c of T = inv(L_kk) by forward substitution on e_c,
-    //   t[i] = -rdiag[i] * sum_{m<i} L[i][m] t[m]  (i > c),  t[c] = rdiag[c],  t[i<c] = 0
+    // threads 0..63: column c of T = inv(L_kk)
     const int c = tid;
     float t[kPB];
+    tile64_inverse_column<kPBLD>(tile, rdiag, c, t);
+    float* tp = Tinv + m * tstride;
 #pragma unroll
-    for (int i = 0; i < kPB; ++i) {
-      const float* rp = tile + i * kPBLD;
-      float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int q = 0; q < i / 4; ++q) {
-        const float4 v = *reinterpret_cast<const float4*>(rp + 4 * q);
-        acc = ffma2(make_float2(v.x, v.y), make_float2(t[4 * q], t[4 * q + 1]), acc);
-        acc = ffma2(make_float2(v.z, v.w), make_float2(t[4 * q + 2], t[4 * q + 3]), acc);
-      }
-      float sum = acc.x + acc.y;
-#pragma unroll
-      for (int mm = (i / 4) * 4; mm < i; ++mm) sum = fmaf(rp[mm], t[mm], sum);
-      const float ri = rdiag[i];
-      t[i] = (i == c) ? ri : ((i < c) ? 0.f : -ri * sum);
-    }
-    float* tp = Tinv + m * (kPB * kPB);
-#pragma unroll
-    for (int i = 0; i < kPB; ++i) tp[i * kPB + c] = t[i];
+    for (int i = 0; i < kPB; ++i) tp[i * tld + c] = t[i];
   }
 }
 
 int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, int64_t stride,
                        int64_t ld, int64_t batch, int64_t k, int64_t kb, float* Tinv, int* info,
-                       cudaStream_t q, bool pdl) {
-  if (kb < 1 || kb > kPB) return CHOL_ERR_UNSUPPORTED;
+                       cudaStream_t q, bool pdl, int64_t tstride, int64_t tld) {
+  if (kb < 1 || kb > kPB || tld < kPB) return CHOL_ERR_UNSUPPORTED;
   if (batch > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
   cudaError_t e = launch_pdl(potrf_block_kernel, dim3(unsigned(batch)), dim3(128), 0, q, pdl, S,
-                             sstride, lds, L, stride, ld, k, int(kb), Tinv, info);
+                             sstride, lds, L, stride, ld, k, int(kb), Tinv, tstride, tld, info);
   return status_from(e);
+}
+
+// =====================================================================================
+// trtri_panel: V = inv(L11) for the KB x KB diagonal block of an outer panel
+// (KB = 64 * nblk), given the diagonal inverses T_j = inv(L_jj) that potrf_block already
+// wrote into V's diagonal blocks. Column block jb of V solves L11 V[:, jb] = E[:, jb] by
+// block forward substitution:
+//   V[jb][jb] = T_jb,   V[i][jb] = -T_i * sum_{k=jb}^{i-1} L[i][k] V[k][jb]   (i > jb).
+// The columns of V are independent, so each CTA owns kTW columns of one column block,
+// keeps its column slice of V in shared memory, and streams the 64 x 64 tiles it needs
+// (L[i][k] for k < i, then T_i) through a two-slot cp.async ring in the order it uses them.
+// It also writes zeros to V's blocks above the diagonal block, so V is a full lower
+// triangle for the GEMM that reads whole rows of it. FP32 FMA throughout.
+// =====================================================================================
+constexpr int kTW = 8;        // V columns per CTA
+constexpr int kTLD = 68;      // ring tile row stride (floats)
+constexpr int kTRing = 64 * kTLD;
+
+size_t trtri_smem(int nblk) {
+  return (size_t(nblk) * 64 * kTW + 2 * kTRing + 64 * kTW) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(128)
+    trtri_panel_kernel(const float* __restrict__ L11, int64_t lstride, int64_t ld,
+                       float* __restrict__ V, int64_t vstride, int64_t ldv, int nblk,
+                       int64_t batch) {
+  extern __shared__ __align__(16) float tsm[];
+  griddep_wait();
+  griddep_launch();
+  const int64_t mi = int64_t(blockIdx.y) + int64_t(blockIdx.z) * 65535;
+  if (mi >= batch) return;
+  float* Vs = tsm;                           // [nblk*64][kTW]: this CTA's column slice
+  float* ring = Vs + nblk * 64 * kTW;        // 2 x [64][kTLD]
+  float* As = ring + 2 * kTRing;             // [64][kTW]: block row sum before T_i
+  constexpr int kPer = 64 / kTW;
+  const int jb = blockIdx.x / kPer;
+  const int c0 = jb * 64 + (blockIdx.x % kPer) * kTW;  // first V column of this CTA
+  const int tid = threadIdx.x;
+  const int r = tid >> 1, cg = (tid & 1) * 4;          // output row, first of 4 columns
+  const float* Lm = L11 + mi * lstride;
+  float* Vm = V + mi * vstride;
+
+  // tile s of the sequence: for i = jb+1.., tiles L[i][k] (k = jb..i-1) then T_i (k == i)
+  auto tile_of = [&](int s, int& ti, int& tk) {
+    int i = jb + 1;
+    while (s > i - jb) {
+      s -= i - jb + 1;
+      ++i;
+    }
+    ti = i;
+    tk = jb + s;
+  };
+  const int total = (nblk - 1 - jb) * (nblk - jb + 2) / 2;
+  auto issue = [&](int s) {
+    int ti, tk;
+    tile_of(s, ti, tk);
+    const float* src = (tk < ti) ? Lm + int64_t(ti) * 64 * ld + tk * 64
+                                 : Vm + int64_t(ti) * 64 * ldv + ti * 64;
+    const int64_t lds = (tk < ti) ? ld : ldv;
+    float* dst = ring + (s & 1) * kTRing;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int idx = tid + e * 128;
+      const int rr = idx >> 4, cc = (idx & 15) * 4;
+      cp_async16(dst + rr * kTLD + cc, src + rr * lds + cc);
+    }
+  };
+
+  if (total > 0) issue(0);
+  cp_async_commit();
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < jb; ++i)
+    *reinterpret_cast<float4*>(Vm + int64_t(i * 64 + r) * ldv + c0 + cg) = z;
+  *reinterpret_cast<float4*>(Vs + (jb * 64 + r) * kTW + cg) =
+      *reinterpret_cast<const float4*>(Vm + int64_t(jb * 64 + r) * ldv + c0 + cg);
+  __syncthreads();
+
+  int s = 0;
+  for (int i = jb + 1; i < nblk; ++i) {
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+    for (int k = jb; k <= i; ++k, ++s) {
+      if (s + 1 < total) issue(s + 1);
+      cp_async_commit();
+      cp_async_wait_group<1>();
+      __syncthreads();
+      const float* tile = ring + (s & 1) * kTRing + r * kTLD;
+      if (k < i) {
+        const float* vk = Vs + k * 64 * kTW + cg;
+#pragma unroll 16
+        for (int kk = 0; kk < 64; ++kk) {
+          const float a = tile[kk];
+          const float4 b = *reinterpret_cast<const float4*>(vk + kk * kTW);
+          acc0 = ffma2(make_float2(a, a), make_float2(b.x, b.y), acc0);
+          acc1 = ffma2(make_float2(a, a), make_float2(b.z, b.w), acc1);
+        }
+      } else {
+        *reinterpret_cast<float4*>(As + r * kTW + cg) = make_float4(acc0.x, acc0.y, acc1.x, acc1.y);
+        __syncthreads();
+        float2 o0 = make_float2(0.f, 0.f), o1 = make_float2(0.f, 0.f);
+#pragma unroll 16
+        for (int kk = 0; kk < 64; ++kk) {  // T_i is lower with zeros above its diagonal
+          const float t = tile[kk];
+          const float4 b = *reinterpret_cast<const float4*>(As + kk * kTW + cg);
+          o0 = ffma2(make_float2(t, t), make_float2(b.x, b.y), o0);
+          o1 = ffma2(make_float2(t, t), make_float2(b.z, b.w), o1);
+        }
+        const float4 o = make_float4(-o0.x, -o0.y, -o1.x, -o1.y);
+        *reinterpret_cast<float4*>(Vs + (i * 64 + r) * kTW + cg) = o;
+        *reinterpret_cast<float4*>(Vm + int64_t(i * 64 + r) * ldv + c0 + cg) = o;
+      }
+      __syncthreads();  // the slot is refilled by the next iteration's issue
+    }
+  }
+  cp_async_wait_group<0>();
+}
+
+cudaError_t prepare_blocked() {
+  return cudaFuncSetAttribute(trtri_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(trtri_smem(16)));
+}
+
+int launch_trtri_panel(const float* L11, int64_t lstride, int64_t ld, float* V, int64_t vstride,
+                       int64_t ldv, int nblk, int64_t batch, cudaStream_t q) {
+  if (nblk < 1 || batch <= 0) return CHOL_OK;
+  if (nblk > 16 || ld % 4 || ldv % 4 || ldv < 64 * nblk) return CHOL_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(L11) & 15) || (reinterpret_cast<uintptr_t>(V) & 15))
+    return CHOL_ERR_UNSUPPORTED;
+  const int64_t gy = batch < 65535 ? batch : 65535;
+  const int64_t gz = (batch + 65534) / 65535;
+  if (gz > 65535) return CHOL_ERR_UNSUPPORTED;
+  const dim3 grid(unsigned(nblk * (64 / kTW)), unsigned(gy), unsigned(gz));
+  return status_from(launch_pdl(trtri_panel_kernel, grid, dim3(128), trtri_smem(nblk), q, true,
+                                L11, lstride, ld, V, vstride, ldv, nblk, batch));
 }
 
 // =====================================================================================

@@ -58,6 +58,14 @@ __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) 
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Wait until at most N of this thread's committed groups are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 // Order this thread's generic-proxy shared-memory writes before async-proxy reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -145,9 +153,23 @@ int prepare_kernels(int device);
 int launch_small(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q);
 int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaStream_t q,
                       bool pdl);
+// Tinv (+ m * tstride, leading dimension tld) receives inv(L_kk) as a 64 x 64 lower triangle.
 int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, int64_t stride,
                        int64_t ld, int64_t batch, int64_t k, int64_t kb, float* Tinv, int* info,
-                       cudaStream_t q, bool pdl);
+                       cudaStream_t q, bool pdl, int64_t tstride = 4096, int64_t tld = 64);
+// One launch: factor the (64 * nb)-square diagonal block at L11 in place and, with want_v,
+// write V = inv(L11) (lower blocks; the caller zeroes the blocks above the diagonal once).
+// flags: kDiagFlags ints per matrix and ticket: one counter, both zero before the first
+// launch; epoch: > 0, distinct for every launch that shares the flags (chol_diag.cu).
+constexpr int kDiagFlags = 768;
+int launch_diag_block(float* L11, int64_t mstride, int64_t ld, float* V, int64_t vstride,
+                      int64_t ldv, int nb, bool want_v, int* flags, unsigned* ticket, int epoch,
+                      int* info, int64_t col0, int64_t batch, cudaStream_t q);
+// V = inv(L11) for a (64 * nblk)-square diagonal block L11 whose 64 x 64 diagonal inverses
+// are already in V's diagonal blocks (chol_blocked.cu).
+cudaError_t prepare_blocked();
+int launch_trtri_panel(const float* L11, int64_t lstride, int64_t ld, float* V, int64_t vstride,
+                       int64_t ldv, int nblk, int64_t batch, cudaStream_t q);
 int launch_gemm_simt(const GemmArgs& g, cudaStream_t q, bool pdl);
 bool tc_supported(const GemmArgs& g);
 // Prebuilt TMA maps over one whole (rows x cols, leading dimension ld) matrix per batch
@@ -168,8 +190,11 @@ int launch_gemm_tc_mapped(const GemmArgs& g, const TcMatrixMaps& pm, const TcMat
 int launch_gemm_tc_mapped_lo(const GemmArgs& g, const TcMatrixMaps& pm, const TcMatrixMaps& qm,
                              const TcMatrixMaps& lm, int64_t lk, cudaStream_t q, bool pdl,
                              int max_ctas = 0);
+// dst = low TF32 part of src (src - its 19-bit truncation); with copy != nullptr, src is also
+// copied to copy (+ m * cstride, leading dimension ldcopy). src and dst may be the same.
 int launch_tf32_lo(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows,
-                   int64_t cols, int64_t batch, int64_t sstride, int64_t dstride, cudaStream_t q);
+                   int64_t cols, int64_t batch, int64_t sstride, int64_t dstride, cudaStream_t q,
+                   float* copy = nullptr, int64_t ldcopy = 0, int64_t cstride = 0);
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status);
 cudaError_t prepare_tc();
 int read_and_clear_status(int* out);
@@ -178,8 +203,11 @@ int* device_status_ptr();
 // Fused 64-wide panel step (chol_panel.cu).
 cudaError_t prepare_panel();
 bool panel_make_map(void* map128, const float* L, int64_t n, int64_t batch);
+// row_end: rows of the panel (default n); tout: optional destination of inv(L_kk).
 int launch_panel_step(const void* map128, float* L, int64_t n, int64_t batch, int64_t k,
-                      int64_t kb, int64_t K0, int* info, unsigned int* counters, cudaStream_t q);
+                      int64_t kb, int64_t K0, int* info, unsigned int* counters, cudaStream_t q,
+                      int64_t row_end = 0, float* tout = nullptr, int64_t tstride = 0,
+                      int64_t tld = 0);
 // Engine choice for the NT-GEMM: 0 auto (tensor cores when the operands allow TMA), 1 FP32
 // FMA only, 2 tensor cores only (CHOL_ERR_UNSUPPORTED where TMA cannot be used).
 extern int g_gemm_engine;

@@ -1,0 +1,368 @@
+// chol_diag.cu — one launch factors an outer panel's diagonal block and inverts it.
+//
+// The KB x KB diagonal block (KB = 64 * nb, nb <= 16) of an outer panel is cut into 64 x 64
+// tiles. Every CTA takes one task from a ticket counter and runs it as soon as the tiles it
+// reads are published:
+//   D(j)    tile (j, j):  C = A_jj - sum_{p<j} L_jp L_jp^T, factor C = L_jj L_jj^T (one
+//           warp), T_j = inv(L_jj); writes L_jj to L and T_j to V's diagonal block.
+//   O(i,j)  tile (i, j), i > j:  L_ij = (A_ij - sum_{p<j} L_ip L_jp^T) T_j^T.
+//   W(i,j)  block (i, j) of V = inv(L11), i > j:  V_ij = -T_i sum_{p=j}^{i-1} L_ip V_pj
+//           (V_jj = T_j), i.e. block forward substitution down column block j.
+// Tasks are numbered so that every task reads only tasks with smaller numbers (D(j), then
+// O(j+1..nb-1, j), column by column; then the W tasks row by row) and matrices of a batch
+// interleave. A CTA learns its task from an atomic ticket, so every task it waits on is
+// held by a CTA that is already running or done: the waits always end, whatever the grid
+// size or residency. A finished task publishes its tile with a release store of the
+// launch's epoch into its flag; readers poll with acquire loads (bounded by a time limit
+// that records CHOL_ERR_WAIT_TIMEOUT in the status word and lets every waiter return) and
+// read tiles through L2 (ld.global.cg).
+//
+// This replaces the per-step chain of the blocked schedule for the block — 3 launches per
+// 64 columns (left-looking GEMM, potrf_block, solve GEMM), each bound by launch and pipeline
+// latency — with one launch whose critical path is the chain of 64 x 64 factors. All
+// arithmetic is FP32 FMA (no TF32 anywhere in the block). The reference factors the same
+// block with its factor/solve/update kernel sequence (cholesky/cholesky.py:5440-5690).
+#include "chol_tc_ptx.cuh"
+#include "chol_warp.cuh"
+
+namespace chol {
+namespace {
+
+constexpr int kDT = 256;   // threads: a 16 x 16 grid of 4 x 4 output blocks
+constexpr int kDLD = 68;   // shared tile row stride (floats)
+constexpr int kFlagO = 256, kFlagW = 512;
+
+struct DiagArgs {
+  float* L;            // (0, 0) of the diagonal block of matrix 0
+  int64_t mstride, ld;
+  float* V;            // V = inv(L11), KB x KB per matrix
+  int64_t vstride, ldv;
+  int* flags;          // kDiagFlags per matrix, zero before the call's first launch
+  unsigned* ticket;    // this launch's ticket counter, zero before the launch
+  int* info;
+  int64_t col0;        // global index of the block's first column (for info)
+  int64_t batch;
+  int nb, want_v, epoch;
+  int* status;
+};
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// All threads: true once *flag == epoch. Thread 0 polls; false (for every thread) when the
+// time limit passes or another CTA has already recorded an error.
+__device__ __forceinline__ bool cta_wait(const int* flag, int epoch, int* status) {
+  int ok = 1;
+  if (threadIdx.x == 0 && ld_acquire(flag) != epoch) {
+    const uint64_t t0 = tcx::global_ns();
+    unsigned ns = 32;
+    for (;;) {
+      __nanosleep(ns);
+      if (ns < 512) ns <<= 1;
+      if (ld_acquire(flag) == epoch) break;
+      if (*reinterpret_cast<volatile int*>(status) != 0) {
+        ok = 0;
+        break;
+      }
+      if (tcx::global_ns() - t0 > tcx::kWaitLimitNs) {
+        atomicExch(status, CHOL_ERR_WAIT_TIMEOUT);
+        ok = 0;
+        break;
+      }
+    }
+  }
+  return __syncthreads_and(ok) != 0;
+}
+
+// Xs[k][r] = X[r][k] for the 64 x 64 tile X (row stride ldx), read through L2.
+__device__ __forceinline__ void stage_t(float* Xs, const float* X, int64_t ldx) {
+  const int t = threadIdx.x;
+  const int r = t & 63, c0 = (t >> 6) * 4;
+  float4 v[4];
+#pragma unroll
+  for (int it = 0; it < 4; ++it)
+    v[it] = __ldcg(reinterpret_cast<const float4*>(X + r * ldx + c0 + 16 * it));
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int c = c0 + 16 * it;
+    Xs[(c + 0) * kDLD + r] = v[it].x;
+    Xs[(c + 1) * kDLD + r] = v[it].y;
+    Xs[(c + 2) * kDLD + r] = v[it].z;
+    Xs[(c + 3) * kDLD + r] = v[it].w;
+  }
+}
+// Ys[k][c] = Y[k][c], read through L2.
+__device__ __forceinline__ void stage_n(float* Ys, const float* Y, int64_t ldy) {
+  const int t = threadIdx.x;
+  const int k = t >> 4, c = (t & 15) * 4;
+  float4 v[4];
+#pragma unroll
+  for (int it = 0; it < 4; ++it)
+    v[it] = __ldcg(reinterpret_cast<const float4*>(Y + (k + 16 * it) * ldy + c));
+#pragma unroll
+  for (int it = 0; it < 4; ++it)
+    *reinterpret_cast<float4*>(Ys + (k + 16 * it) * kDLD + c) = v[it];
+}
+
+// acc[i] (row 4tr+i; .x/.y of [i][0] = columns 4tc, 4tc+1, of [i][1] = 4tc+2, 4tc+3)
+//   += sum_k Xs[k][4tr+i] * Ys[k][4tc+j]
+__device__ __forceinline__ void tile_fma(float2 (&acc)[4][2], const float* Xs, const float* Ys,
+                                         int tr, int tc) {
+#pragma unroll 8
+  for (int k = 0; k < 64; ++k) {
+    const float4 a = *reinterpret_cast<const float4*>(Xs + k * kDLD + 4 * tr);
+    const float4 b = *reinterpret_cast<const float4*>(Ys + k * kDLD + 4 * tc);
+    const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
+    acc[0][0] = ffma2(make_float2(a.x, a.x), b01, acc[0][0]);
+    acc[0][1] = ffma2(make_float2(a.x, a.x), b23, acc[0][1]);
+    acc[1][0] = ffma2(make_float2(a.y, a.y), b01, acc[1][0]);
+    acc[1][1] = ffma2(make_float2(a.y, a.y), b23, acc[1][1]);
+    acc[2][0] = ffma2(make_float2(a.z, a.z), b01, acc[2][0]);
+    acc[2][1] = ffma2(make_float2(a.z, a.z), b23, acc[2][1]);
+    acc[3][0] = ffma2(make_float2(a.w, a.w), b01, acc[3][0]);
+    acc[3][1] = ffma2(make_float2(a.w, a.w), b23, acc[3][1]);
+  }
+}
+
+// This thread's 4 x 4 block of a 64 x 64 global tile (row stride ld).
+__device__ __forceinline__ void load_block(float4 (&v)[4], const float* X, int64_t ld, int tr,
+                                           int tc) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    v[i] = __ldcg(reinterpret_cast<const float4*>(X + (4 * tr + i) * ld + 4 * tc));
+}
+__device__ __forceinline__ void store_block(float* X, int64_t ld, const float2 (&acc)[4][2],
+                                            float sign, int tr, int tc) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<float4*>(X + (4 * tr + i) * ld + 4 * tc) =
+        make_float4(sign * acc[i][0].x, sign * acc[i][0].y, sign * acc[i][1].x,
+                    sign * acc[i][1].y);
+}
+
+__device__ __forceinline__ void zero(float2 (&acc)[4][2]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
+}
+
+// Task number -> (type, i, j): 0 = D(j), 1 = O(i, j), 2 = W(i, j).
+__device__ __forceinline__ void decode_task(int t, int nb, int& type, int& i, int& j) {
+  const int nL = nb * (nb + 1) / 2;
+  if (t < nL) {
+    j = 0;
+    while (t >= nb - j) {
+      t -= nb - j;
+      ++j;
+    }
+    i = j + t;
+    type = (t == 0) ? 0 : 1;
+    return;
+  }
+  t -= nL;
+  i = 1;
+  while (t >= i) {
+    t -= i;
+    ++i;
+  }
+  j = t;
+  type = 2;
+}
+
+__global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
+  __shared__ __align__(16) float Xs[64 * kDLD];
+  __shared__ __align__(16) float Ys[64 * kDLD];
+  __shared__ __align__(16) float col[128];
+  __shared__ float rdiag[64];
+  __shared__ unsigned s_ticket;
+  __shared__ int s_fail;
+  griddep_wait();
+  const int tid = threadIdx.x;
+  if (tid == 0) s_ticket = atomicAdd(a.ticket, 1u);
+  __syncthreads();
+  griddep_launch();
+  const int64_t tk = s_ticket;
+  const int64_t task = tk / a.batch, mi = tk - task * a.batch;
+  const int nb = a.nb;
+  const int ntask = nb * (nb + 1) / 2 + (a.want_v ? nb * (nb - 1) / 2 : 0);
+  if (task >= ntask) return;
+  int type, i, j;
+  decode_task(int(task), nb, type, i, j);
+
+  float* Lm = a.L + mi * a.mstride;
+  float* Vm = a.V + mi * a.vstride;
+  int* F = a.flags + mi * kDiagFlags;
+  const int ep = a.epoch;
+  const int64_t ld = a.ld, ldv = a.ldv;
+  auto tileL = [&](int bi, int bj) { return Lm + int64_t(bi) * 64 * ld + bj * 64; };
+  auto tileV = [&](int bi, int bj) { return Vm + int64_t(bi) * 64 * ldv + bj * 64; };
+  const int tr = tid >> 4, tc = tid & 15;
+  float2 acc[4][2];
+  zero(acc);
+  int* my_flag;
+
+  if (type == 0) {
+    // ---------------- D(j) ----------------
+    float4 av[4];
+    load_block(av, tileL(j, j), ld, tr, tc);
+    for (int p = 0; p < j; ++p) {
+      if (!cta_wait(&F[kFlagO + j * 16 + p], ep, a.status)) return;
+      stage_t(Xs, tileL(j, p), ld);
+      __syncthreads();
+      tile_fma(acc, Xs, Xs, tr, tc);
+      __syncthreads();
+    }
+    // S = A - acc (lower part; zeros above the diagonal) into Ys
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int r = 4 * tr + u, c = 4 * tc;
+      float4 o = make_float4(av[u].x - acc[u][0].x, av[u].y - acc[u][0].y,
+                             av[u].z - acc[u][1].x, av[u].w - acc[u][1].y);
+      if (c + 0 > r) o.x = 0.f;
+      if (c + 1 > r) o.y = 0.f;
+      if (c + 2 > r) o.z = 0.f;
+      if (c + 3 > r) o.w = 0.f;
+      *reinterpret_cast<float4*>(Ys + r * kDLD + c) = o;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      const int f = tile64_potrf<kDLD>(Ys, col, rdiag, tid);
+      if (tid == 0) s_fail = f;
+    }
+    __syncthreads();
+    if (tid < 64) {
+      float t[64];
+      tile64_inverse_column<kDLD>(Ys, rdiag, tid, t);
+#pragma unroll
+      for (int r = 0; r < 64; ++r) Xs[r * kDLD + tid] = t[r];
+    } else {
+      float* dst = tileL(j, j);
+      for (int e = tid - 64; e < 64 * 16; e += kDT - 64) {
+        const int r = e >> 4, c = (e & 15) * 4;
+        *reinterpret_cast<float4*>(dst + r * ld + c) =
+            *reinterpret_cast<const float4*>(Ys + r * kDLD + c);
+      }
+    }
+    __syncthreads();
+    {
+      float* dst = tileV(j, j);
+      for (int e = tid; e < 64 * 16; e += kDT) {
+        const int r = e >> 4, c = (e & 15) * 4;
+        *reinterpret_cast<float4*>(dst + r * ldv + c) =
+            *reinterpret_cast<const float4*>(Xs + r * kDLD + c);
+      }
+    }
+    if (tid == 0 && a.info != nullptr) {
+      const int64_t c0 = a.col0 + int64_t(j) * 64;
+      const int f = s_fail;
+      if (c0 == 0)
+        a.info[mi] = f;
+      else if (f && a.info[mi] == 0)
+        a.info[mi] = int(c0) + f;
+    }
+    my_flag = &F[j];
+  } else if (type == 1) {
+    // ---------------- O(i, j) ----------------
+    float4 av[4];
+    load_block(av, tileL(i, j), ld, tr, tc);
+    for (int p = 0; p < j; ++p) {
+      if (!cta_wait(&F[kFlagO + i * 16 + p], ep, a.status)) return;
+      if (!cta_wait(&F[kFlagO + j * 16 + p], ep, a.status)) return;
+      stage_t(Xs, tileL(i, p), ld);
+      stage_t(Ys, tileL(j, p), ld);
+      __syncthreads();
+      tile_fma(acc, Xs, Ys, tr, tc);
+      __syncthreads();
+    }
+    // C = A - acc, transposed into Xs (Xs[c][r] = C[r][c]) for the solve
+    {
+      float cv[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        cv[u][0] = av[u].x - acc[u][0].x;
+        cv[u][1] = av[u].y - acc[u][0].y;
+        cv[u][2] = av[u].z - acc[u][1].x;
+        cv[u][3] = av[u].w - acc[u][1].y;
+      }
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        *reinterpret_cast<float4*>(Xs + (4 * tc + v) * kDLD + 4 * tr) =
+            make_float4(cv[0][v], cv[1][v], cv[2][v], cv[3][v]);
+    }
+    if (!cta_wait(&F[j], ep, a.status)) return;
+    stage_t(Ys, tileV(j, j), ldv);  // Ys[k][c] = T_j[c][k]
+    __syncthreads();
+    zero(acc);
+    tile_fma(acc, Xs, Ys, tr, tc);
+    store_block(tileL(i, j), ld, acc, 1.f, tr, tc);
+    my_flag = &F[kFlagO + i * 16 + j];
+  } else {
+    // ---------------- W(i, j) ----------------
+    for (int p = j; p < i; ++p) {
+      if (!cta_wait(&F[kFlagO + i * 16 + p], ep, a.status)) return;
+      if (!cta_wait(p == j ? &F[j] : &F[kFlagW + p * 16 + j], ep, a.status)) return;
+      stage_t(Xs, tileL(i, p), ld);
+      stage_n(Ys, tileV(p, j), ldv);
+      __syncthreads();
+      tile_fma(acc, Xs, Ys, tr, tc);
+      __syncthreads();
+    }
+    // Ys = the sum (row-major), Xs[k][r] = T_i[r][k]
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      *reinterpret_cast<float4*>(Ys + (4 * tr + u) * kDLD + 4 * tc) =
+          make_float4(acc[u][0].x, acc[u][0].y, acc[u][1].x, acc[u][1].y);
+    if (!cta_wait(&F[i], ep, a.status)) return;
+    stage_t(Xs, tileV(i, i), ldv);
+    __syncthreads();
+    zero(acc);
+    tile_fma(acc, Xs, Ys, tr, tc);
+    store_block(tileV(i, j), ldv, acc, -1.f, tr, tc);
+    my_flag = &F[kFlagW + i * 16 + j];
+  }
+  // publish: every thread's stores, then the flag (release at GPU scope)
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    st_release(my_flag, ep);
+  }
+}
+
+}  // namespace
+
+int launch_diag_block(float* L11, int64_t mstride, int64_t ld, float* V, int64_t vstride,
+                      int64_t ldv, int nb, bool want_v, int* flags, unsigned* ticket, int epoch,
+                      int* info, int64_t col0, int64_t batch, cudaStream_t q) {
+  if (nb < 1 || batch <= 0) return CHOL_OK;
+  if (nb > 16 || ld % 4 || ldv % 4 || ldv < 64 * nb || epoch <= 0) return CHOL_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(L11) & 15) || (reinterpret_cast<uintptr_t>(V) & 15))
+    return CHOL_ERR_UNSUPPORTED;
+  DiagArgs a{};
+  a.L = L11;
+  a.mstride = mstride;
+  a.ld = ld;
+  a.V = V;
+  a.vstride = vstride;
+  a.ldv = ldv;
+  a.flags = flags;
+  a.ticket = ticket;
+  a.info = info;
+  a.col0 = col0;
+  a.batch = batch;
+  a.nb = nb;
+  a.want_v = want_v ? 1 : 0;
+  a.epoch = epoch;
+  a.status = device_status_ptr();
+  if (a.status == nullptr) return CHOL_ERR_DEVICE;
+  const int64_t ntask = int64_t(nb) * (nb + 1) / 2 + (want_v ? int64_t(nb) * (nb - 1) / 2 : 0);
+  const int64_t ctas = ntask * batch;
+  if (ctas > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
+  return status_from(launch_pdl(diag_block_kernel, dim3(unsigned(ctas)), dim3(kDT), 0, q, true, a));
+}
+
+}  // namespace chol

@@ -39,11 +39,13 @@ constexpr size_t kPS_Smem = size_t(kPS_Work) + 1024 + 1024;
 
 struct PanelArgs {
   float* L;
-  int64_t n, ld, mstride, batch;
+  int64_t n, ld, mstride, batch;  // n: rows of the panel (row limit), ld: row stride
   int64_t k, kb, K0;
   int* info;
   unsigned int* counters;  // one per matrix, zero between launches
   int* status;
+  float* tout;             // optional: inv(L_kk) (+ m * tstride, leading dimension tld)
+  int64_t tstride, tld;
 };
 
 __device__ __forceinline__ void named_sync_128() {
@@ -327,11 +329,19 @@ __global__ void __launch_bounds__(kPS_Threads, 2)
       }
     }
 
-    // ---- the last CTA of the matrix writes the diagonal block and info ----
+    // ---- the last CTA of the matrix writes the diagonal block, its inverse and info ----
     if (flags[1]) {
       for (int idx = et; idx < kb * kb; idx += 128) {
         const int i = idx / int(kb), c = idx - i * int(kb);
         Lm[(k + i) * a.ld + k + c] = S[i * kPS_SLD + c];
+      }
+      if (a.tout != nullptr) {
+        float* tm = a.tout + mi * a.tstride;
+        for (int idx = et; idx < 64 * 16; idx += 128) {
+          const int i = idx >> 4, c = (idx & 15) * 4;
+          *reinterpret_cast<float4*>(tm + i * a.tld + c) =
+              *reinterpret_cast<const float4*>(T + i * kPS_SLD + c);
+        }
       }
       if (et == 0 && a.info != nullptr) {
         const int f = flags[0] > kb ? 0 : flags[0];
@@ -383,11 +393,18 @@ bool panel_make_map(void* map128, const float* L, int64_t n, int64_t batch) {
 }
 
 int launch_panel_step(const void* map128, float* L, int64_t n, int64_t batch, int64_t k,
-                      int64_t kb, int64_t K0, int* info, unsigned int* counters, cudaStream_t q) {
+                      int64_t kb, int64_t K0, int* info, unsigned int* counters, cudaStream_t q,
+                      int64_t row_end, float* tout, int64_t tstride, int64_t tld) {
+  if (row_end <= 0 || row_end > n) row_end = n;
+  if (tout != nullptr && (tld % 4 || (reinterpret_cast<uintptr_t>(tout) & 15)))
+    return CHOL_ERR_UNSUPPORTED;
   PanelArgs a{};
   a.L = L;
-  a.n = n;
+  a.n = row_end;
   a.ld = n;
+  a.tout = tout;
+  a.tstride = tstride;
+  a.tld = tld;
   a.mstride = n * n;
   a.batch = batch;
   a.k = k;
@@ -397,7 +414,7 @@ int launch_panel_step(const void* map128, float* L, int64_t n, int64_t batch, in
   a.counters = counters;
   a.status = device_status_ptr();
   if (a.status == nullptr) return CHOL_ERR_DEVICE;
-  const int64_t below = n - k - kb;
+  const int64_t below = row_end - k - kb;
   const int64_t tiles = below > 0 ? (below + 63) / 64 : 1;
   const int64_t by = batch < 65535 ? batch : 65535;
   const int64_t bz = (batch + 65534) / 65535;

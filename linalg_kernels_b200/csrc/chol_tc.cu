@@ -586,10 +586,11 @@ cudaError_t set_tc_smem() {
 }
 
 // lo = x - trunc_tf32(x) for a rows x cols view (float4 columns; cols % 4 == 0).
-__global__ void __launch_bounds__(256) tf32_lo_kernel(const float* __restrict__ src, int64_t lds,
-                                                      float* __restrict__ dst, int64_t ldd,
-                                                      int64_t rows, int64_t cols4, int64_t batch,
-                                                      int64_t sstride, int64_t dstride) {
+__global__ void __launch_bounds__(256) tf32_lo_kernel(const float* src, int64_t lds, float* dst,
+                                                      int64_t ldd, int64_t rows, int64_t cols4,
+                                                      int64_t batch, int64_t sstride,
+                                                      int64_t dstride, float* copy,
+                                                      int64_t ldcopy, int64_t cstride) {
   griddep_wait();
   griddep_launch();
   const int64_t total = batch * rows * cols4;
@@ -604,6 +605,7 @@ __global__ void __launch_bounds__(256) tf32_lo_kernel(const float* __restrict__ 
     l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
     l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
     l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+    if (copy != nullptr) *reinterpret_cast<float4*>(copy + m * cstride + r * ldcopy + 4 * c4) = x;
     *reinterpret_cast<float4*>(dst + m * dstride + r * ldd + 4 * c4) = l;
   }
 }
@@ -621,15 +623,18 @@ cudaError_t prepare_tc() {
 }
 
 int launch_tf32_lo(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows,
-                   int64_t cols, int64_t batch, int64_t sstride, int64_t dstride, cudaStream_t q) {
+                   int64_t cols, int64_t batch, int64_t sstride, int64_t dstride, cudaStream_t q,
+                   float* copy, int64_t ldcopy, int64_t cstride) {
   if (rows <= 0 || cols <= 0 || batch <= 0) return CHOL_OK;
-  if (cols % 4 || lds % 4 || ldd % 4) return CHOL_ERR_UNSUPPORTED;
+  if (cols % 4 || lds % 4 || ldd % 4 || (copy != nullptr && ldcopy % 4))
+    return CHOL_ERR_UNSUPPORTED;
   const int64_t work = batch * rows * (cols / 4);
   int64_t blocks = (work + 255) / 256;
   const int64_t cap = int64_t(g_num_sms > 0 ? g_num_sms : 148) * 16;
   if (blocks > cap) blocks = cap;
   return status_from(launch_pdl(tf32_lo_kernel, dim3(unsigned(blocks)), dim3(256), 0, q, true,
-                                src, lds, dst, ldd, rows, cols / 4, batch, sstride, dstride));
+                                src, lds, dst, ldd, rows, cols / 4, batch, sstride, dstride, copy,
+                                ldcopy, cstride));
 }
 
 int* device_status_ptr() {

@@ -113,4 +113,77 @@ __device__ __forceinline__ void warp_potrf_rows(uint64_t (&a)[NP / LPM_][NP / 2]
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// 64 x 64 diagonal-block helpers shared by the block kernels. `tile` is row-major in shared
+// memory with row stride LD (a multiple of 4 floats); the lower triangle holds the block.
+
+// One warp factors the block in place: lower triangle of L, exact zeros above the
+// diagonal. rdiag receives 1 / L[i][i]. Returns in every lane the 1-based index of the
+// first column whose pivot is not > 0 (NaN included), or 0.
+template <int LD>
+__device__ __forceinline__ int tile64_potrf(float* tile, float* col, float* rdiag, int lane) {
+  uint64_t a[2][32];
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const float* rp = tile + (s * 32 + lane) * LD;
+#pragma unroll
+    for (int q = 0; q < (s + 1) * 8; ++q) {
+      const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(rp + 4 * q);
+      a[s][2 * q] = v.x;
+      a[s][2 * q + 1] = v.y;
+    }
+  }
+  warp_potrf_rows<64>(a, col, lane);
+  __syncwarp();
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const int i = s * 32 + lane;
+    float* rp = tile + i * LD;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (4 * q < (s + 1) * 32) {
+        v.x = (4 * q + 0 <= i) ? lo_of(a[s][2 * q]) : 0.f;
+        v.y = (4 * q + 1 <= i) ? hi_of(a[s][2 * q]) : 0.f;
+        v.z = (4 * q + 2 <= i) ? lo_of(a[s][2 * q + 1]) : 0.f;
+        v.w = (4 * q + 3 <= i) ? hi_of(a[s][2 * q + 1]) : 0.f;
+      }
+      *reinterpret_cast<float4*>(rp + 4 * q) = v;
+    }
+  }
+  __syncwarp();
+  const float d0 = tile[lane * LD + lane];
+  const float d1 = tile[(lane + 32) * LD + lane + 32];
+  rdiag[lane] = __frcp_rn(d0);
+  rdiag[lane + 32] = __frcp_rn(d1);
+  const unsigned b0 = __ballot_sync(0xffffffffu, !(d0 > 0.f));
+  const unsigned b1 = __ballot_sync(0xffffffffu, !(d1 > 0.f));
+  __syncwarp();
+  return b0 ? __ffs(b0) : (b1 ? 32 + __ffs(b1) : 0);
+}
+
+// Column c of T = inv(L) for the factored block (one thread per column), by forward
+// substitution on e_c:  t[i] = -rdiag[i] * sum_{m<i} L[i][m] t[m] (i > c), t[c] = rdiag[c],
+// t[i] = 0 (i < c).
+template <int LD>
+__device__ __forceinline__ void tile64_inverse_column(const float* tile, const float* rdiag,
+                                                      int c, float (&t)[64]) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    const float* rp = tile + i * LD;
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < i / 4; ++q) {
+      const float4 v = *reinterpret_cast<const float4*>(rp + 4 * q);
+      acc = ffma2(make_float2(v.x, v.y), make_float2(t[4 * q], t[4 * q + 1]), acc);
+      acc = ffma2(make_float2(v.z, v.w), make_float2(t[4 * q + 2], t[4 * q + 3]), acc);
+    }
+    float sum = acc.x + acc.y;
+#pragma unroll
+    for (int mm = (i / 4) * 4; mm < i; ++mm) sum = fmaf(rp[mm], t[mm], sum);
+    const float ri = rdiag[i];
+    t[i] = (i == c) ? ri : ((i < c) ? 0.f : -ri * sum);
+  }
+}
+
 }  // namespace chol

@@ -98,12 +98,16 @@ def test_diagonal_known_answer():
 def _check_full_config(name, batch=None):
     cfg = inputs.CONFIGS[name]
     a, cond = inputs.config_input(cfg, device=DEV, batch=batch)
+    return _check_input(a, cond)
+
+
+def _check_input(a, cond):
     a_before = a.clone()
     l = custom_kernel(a)
     l_ref = torch.linalg.cholesky_ex(a, check_errors=False).L  # the reference path on GPU
     torch.cuda.synchronize()
     assert torch.equal(a, a_before), "input was modified"
-    n = cfg.n
+    n = a.shape[-1]
     assert torch.isfinite(l).all()
     assert (torch.triu(l, 1) == 0).all()
     assert (l.diagonal(dim1=-2, dim2=-1) > 0).all()
@@ -211,11 +215,50 @@ def test_fused_panel_step_option(name):
         lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, -1)
 
 
-def test_three_launch_step_at_large_n():
-    """n = 16384 through the three-launch step (the default there is the fused step)."""
+def test_row_chain_panel_solve_at_large_n():
+    """n = 16384 with the panel solved by 64-wide steps over every row of the panel
+    (CHOL_OPT_PANEL_INVERSE = 0) instead of one GEMM with the diagonal block's inverse."""
     lib = _lib.load()
-    lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, 0)
+    lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 0)
     try:
         _check_full_config("b1n16384")
     finally:
+        lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)
+
+
+# n > 1024: several 512-wide outer panels. 1536/2048: whole panels; 2100: a 52-wide last
+# panel; 1030, 2050: rows that are not 16-byte multiples (the schedule without the optional
+# panel buffer). Spectral inputs up to cond 1e5 exercise the inverse-based panel solve.
+@pytest.mark.parametrize("batch,n,lam", [(1, 1536, 1e3), (3, 2048, 1e4), (1, 2100, 1e5),
+                                         (2, 1030, 1e3), (1, 2050, 1e4), (1, 4096, 1e5)])
+@pytest.mark.parametrize("panel_inverse,fused", [(1, 0), (2, 0), (0, 0), (2, 1)])
+def test_multi_panel_sizes(batch, n, lam, panel_inverse, fused):
+    lib = _lib.load()
+    lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, panel_inverse)
+    lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, fused)
+    try:
+        a, cond = inputs.spectral(batch, n, lam, 7000 + n, device=DEV)
+        _check_input(a, cond)
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)
         lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, -1)
+
+
+@pytest.mark.parametrize("n", [2048, 3072])
+def test_lookahead_matches_in_order_schedule(n):
+    """The side-queue look-ahead (CHOL_OPT_LOOKAHEAD) only reorders independent work:
+    bitwise the same factor as the in-order schedule, with and without the panel inverse."""
+    lib = _lib.load()
+    a, _ = inputs.covariance(2, n, 0.5, 9000 + n, device=DEV)
+    try:
+        for inv in (1, 0):
+            lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, inv)
+            lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 0)
+            want = custom_kernel(a)
+            lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 1)
+            got = custom_kernel(a)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), inv
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 0)
+        lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)

@@ -133,9 +133,10 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
 /*   CHOL_OPT_OUTER_WIDTH: width of the outer panels of the blocked path (multiple of 64;
  *   0 = default: n for n <= 1024, else 512). */
 #define CHOL_OPT_OUTER_WIDTH 3
-/*   CHOL_OPT_LOOKAHEAD: 1 = for large n, the trailing update of each outer panel runs on a
- *   library side queue beside the next panel's factorisation (the call still completes on
- *   the caller's queue); 0 (default) = everything in order on the caller's queue.
+/*   CHOL_OPT_LOOKAHEAD: 1 = for large n, most of the trailing update of an outer panel runs
+ *   on a library side queue beside the next panel's factorisation, for the panels whose
+ *   update is short enough for the overlap to pay (the call still completes on the
+ *   caller's queue); 0 (default) = everything in order on the caller's queue.
  *   CHOL_OPT_CHAIN_SMS: SMs the side-queue update leaves free for the panel chain (24). */
 #define CHOL_OPT_LOOKAHEAD 4
 #define CHOL_OPT_CHAIN_SMS 5

@@ -131,10 +131,19 @@ int gemm_on(const GemmArgs& g, const BlockedMaps& bm, const TcMatrixMaps& pm,
 
 // Look-ahead between outer panels (large n): the trailing update of panel J is split into
 // T1 (panel J+1's own columns, on the caller's queue) and T2 (everything to its right, on a
-// library side queue with its grid capped so that kChainSms SMs stay free); panel J+1's
-// chain of small kernels then runs beside T2.
+// library side queue with its grid capped so that g_chain_sms SMs stay free); panel J+1's
+// diagonal block, panel solve and split then run beside T2. The cap slows T2 by about
+// sms / (sms - g_chain_sms), so the split is taken only while T2 is short enough for the
+// overlap to win: batch * rest^2 <= kLookaheadWork (rest = rows below the next panel; about
+// 1 ms of T2 on a B200 against ~0.2 ms of per-panel chain).
 int g_lookahead = 0;
 int g_chain_sms = 24;
+constexpr double kLookaheadWork = 4.0e8;
+
+bool lookahead_split(int64_t batch, int64_t rest_after_next) {
+  return g_lookahead && rest_after_next > 0 &&
+         double(batch) * double(rest_after_next) * double(rest_after_next) <= kLookaheadWork;
+}
 
 struct SideQueue {
   std::once_flag once;
@@ -356,7 +365,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
     if (st) return st;
     const int64_t K0n = K0 + KB;
     const int64_t KBn = rest < NBw ? rest : NBw;
-    if (sq != nullptr && rest > KBn) {
+    if (sq != nullptr && rest > KBn && lookahead_split(batch, rest - KBn)) {
       // T1: next panel's columns, here; T2: the rest, on the side queue
       GemmArgs t1 = t;
       t1.ncols = KBn;
@@ -418,7 +427,7 @@ int64_t blocked_launches(int64_t batch, int64_t n, bool fused) {
     }
     count += inv ? (one_launch ? 2 : 3) : 1;     // ((trtri +) solve GEMM +) split/lo pass
     count += 1;                                  // trailing update
-    if (g_lookahead && rest > NB) count += 1;    // split into T1 + T2
+    if (rest > NB && lookahead_split(batch, rest - NB)) count += 1;  // T1 + T2
   }
   return count;
 }

@@ -3,19 +3,28 @@
 // The KB x KB diagonal block (KB = 64 * nb, nb <= 16) of an outer panel is cut into 64 x 64
 // tiles. Every CTA takes one task from a ticket counter and runs it as soon as the tiles it
 // reads are published:
-//   D(j)    tile (j, j):  C = A_jj - sum_{p<j} L_jp L_jp^T, factor C = L_jj L_jj^T (one
-//           warp), T_j = inv(L_jj); writes L_jj to L and T_j to V's diagonal block.
-//   O(i,j)  tile (i, j), i > j:  L_ij = (A_ij - sum_{p<j} L_ip L_jp^T) T_j^T.
-//   W(i,j)  block (i, j) of V = inv(L11), i > j:  V_ij = -T_i sum_{p=j}^{i-1} L_ip V_pj
-//           (V_jj = T_j), i.e. block forward substitution down column block j.
-// Tasks are numbered so that every task reads only tasks with smaller numbers (D(j), then
-// O(j+1..nb-1, j), column by column; then the W tasks row by row) and matrices of a batch
-// interleave. A CTA learns its task from an atomic ticket, so every task it waits on is
-// held by a CTA that is already running or done: the waits always end, whatever the grid
-// size or residency. A finished task publishes its tile with a release store of the
+//   D(0)      tile (0, 0): factor A_00 = L_00 L_00^T, T_0 = inv(L_00).
+//   O(i,j)    tile (i, j), i > j:  L_ij = (A_ij - sum_{p<j} L_ip L_jp^T) T_j^T. For i = j + 1
+//             the same CTA then factors the next diagonal tile,
+//               A_ii - sum_{p<=j} L_ip L_ip^T = L_ii L_ii^T,  T_i = inv(L_ii)
+//             reusing the L_ip tiles it already staged (this is the critical path: the task
+//             that produces L_{j+1,j} goes straight on to the factor that needs it).
+//   W(i,j)    block (i, j) of V = inv(L11), i > j:  V_ij = -T_i sum_{p=j}^{i-1} L_ip V_pj
+//             (V_jj = T_j), i.e. block forward substitution down column block j.
+// L_jj goes to L and T_j to V's diagonal block.
+// Tasks are numbered so that every task reads only tasks with smaller numbers (column by
+// column: D(0), O(1..nb-1, 0), O(2..nb-1, 1), ...; then the W tasks row by row) and matrices
+// of a batch interleave. A CTA learns its task from an atomic ticket, so every task it
+// waits on is held by a CTA that is already running or done: the waits always end, whatever
+// the grid size or residency. A finished tile is published by a release store of the
 // launch's epoch into its flag; readers poll with acquire loads (bounded by a time limit
 // that records CHOL_ERR_WAIT_TIMEOUT in the status word and lets every waiter return) and
 // read tiles through L2 (ld.global.cg).
+//
+// Factors: the register-resident warp factor (warp_potrf_rows) and the column-parallel
+// inverse are fully unrolled, several thousand instructions that a task runs once. The
+// diagonal tasks after D(0) run both once on scratch data while they wait for their inputs,
+// so the real run starts with this SM's instruction cache warm.
 //
 // This replaces the per-step chain of the blocked schedule for the block — 3 launches per
 // 64 columns (left-looking GEMM, potrf_block, solve GEMM), each bound by launch and pipeline
@@ -61,10 +70,8 @@ __device__ __forceinline__ bool cta_wait(const int* flag, int epoch, int* status
   int ok = 1;
   if (threadIdx.x == 0 && ld_acquire(flag) != epoch) {
     const uint64_t t0 = tcx::global_ns();
-    unsigned ns = 32;
     for (;;) {
-      __nanosleep(ns);
-      if (ns < 512) ns <<= 1;
+      __nanosleep(32);
       if (ld_acquire(flag) == epoch) break;
       if (*reinterpret_cast<volatile int*>(status) != 0) {
         ok = 0;
@@ -151,20 +158,28 @@ __device__ __forceinline__ void zero(float2 (&acc)[4][2]) {
   for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
 }
 
-// Task number -> (type, i, j): 0 = D(j), 1 = O(i, j), 2 = W(i, j).
+// Task number -> (type, i, j): 0 = D(0), 1 = O(i, j) (with the factor of tile (i, i) when
+// i == j + 1), 2 = W(i, j).
 __device__ __forceinline__ void decode_task(int t, int nb, int& type, int& i, int& j) {
-  const int nL = nb * (nb + 1) / 2;
-  if (t < nL) {
+  if (t < nb) {  // column 0: D(0), O(1, 0), ..., O(nb-1, 0)
     j = 0;
-    while (t >= nb - j) {
-      t -= nb - j;
-      ++j;
-    }
-    i = j + t;
+    i = t;
     type = (t == 0) ? 0 : 1;
     return;
   }
-  t -= nL;
+  t -= nb;
+  const int nO = nb * (nb - 1) / 2 - (nb - 1);  // O tasks of columns 1 .. nb-2
+  if (t < nO) {
+    j = 1;
+    while (t >= nb - 1 - j) {
+      t -= nb - 1 - j;
+      ++j;
+    }
+    i = j + 1 + t;
+    type = 1;
+    return;
+  }
+  t -= nO;
   i = 1;
   while (t >= i) {
     t -= i;
@@ -174,13 +189,70 @@ __device__ __forceinline__ void decode_task(int t, int nb, int& type, int& i, in
   type = 2;
 }
 
+// S = this thread's 4 x 4 block of (A - acc), lower part only (zeros above the diagonal).
+__device__ __forceinline__ void put_lower(float* S, const float4 (&av)[4],
+                                          const float2 (&acc)[4][2], int tr, int tc) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int r = 4 * tr + u, c = 4 * tc;
+    float4 o = make_float4(av[u].x - acc[u][0].x, av[u].y - acc[u][0].y,
+                           av[u].z - acc[u][1].x, av[u].w - acc[u][1].y);
+    if (c + 0 > r) o.x = 0.f;
+    if (c + 1 > r) o.y = 0.f;
+    if (c + 2 > r) o.z = 0.f;
+    if (c + 3 > r) o.w = 0.f;
+    *reinterpret_cast<float4*>(S + r * kDLD + c) = o;
+  }
+}
+// Xs[c][r] = this thread's 4 x 4 block of M (transposed store).
+__device__ __forceinline__ void put_transposed(float* Xs, const float (&m)[4][4], int tr,
+                                               int tc) {
+#pragma unroll
+  for (int v = 0; v < 4; ++v)
+    *reinterpret_cast<float4*>(Xs + (4 * tc + v) * kDLD + 4 * tr) =
+        make_float4(m[0][v], m[1][v], m[2][v], m[3][v]);
+}
+__device__ __forceinline__ void to_array(float (&m)[4][4], const float2 (&acc)[4][2]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    m[u][0] = acc[u][0].x;
+    m[u][1] = acc[u][0].y;
+    m[u][2] = acc[u][1].x;
+    m[u][3] = acc[u][1].y;
+  }
+}
+
+// The unrolled warp factor and the column-parallel inverse, each as ONE function: every call
+// site (and the warm-up run) executes the same instructions, and their register needs stay
+// apart from the task code around them.
+__device__ __noinline__ int warp_factor64(float* S, float* col, float* rdiag, int lane) {
+  return tile64_potrf<kDLD>(S, col, rdiag, lane);
+}
+// Column c of T = inv(L) into Ts (row-major, stride kDLD), one thread per column.
+__device__ __noinline__ void inverse_column64(const float* S, const float* rdiag, float* Ts,
+                                              int c) {
+  float t[64];
+  tile64_inverse_column<kDLD>(S, rdiag, c, t);
+#pragma unroll
+  for (int r = 0; r < 64; ++r) Ts[r * kDLD + c] = t[r];
+}
+
+// Publish: every thread's global stores, then the flag (release at GPU scope).
+__device__ __forceinline__ void publish(int* flag, int epoch) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    st_release(flag, epoch);
+  }
+}
+
 __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   __shared__ __align__(16) float Xs[64 * kDLD];
   __shared__ __align__(16) float Ys[64 * kDLD];
   __shared__ __align__(16) float col[128];
   __shared__ float rdiag[64];
   __shared__ unsigned s_ticket;
-  __shared__ int s_fail;
+  __shared__ int s_flag[1];
   griddep_wait();
   const int tid = threadIdx.x;
   if (tid == 0) s_ticket = atomicAdd(a.ticket, 1u);
@@ -189,7 +261,7 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   const int64_t tk = s_ticket;
   const int64_t task = tk / a.batch, mi = tk - task * a.batch;
   const int nb = a.nb;
-  const int ntask = nb * (nb + 1) / 2 + (a.want_v ? nb * (nb - 1) / 2 : 0);
+  const int ntask = 1 + nb * (nb - 1) / 2 + (a.want_v ? nb * (nb - 1) / 2 : 0);
   if (task >= ntask) return;
   int type, i, j;
   decode_task(int(task), nb, type, i, j);
@@ -202,74 +274,34 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   auto tileL = [&](int bi, int bj) { return Lm + int64_t(bi) * 64 * ld + bj * 64; };
   auto tileV = [&](int bi, int bj) { return Vm + int64_t(bi) * 64 * ldv + bj * 64; };
   const int tr = tid >> 4, tc = tid & 15;
+
   float2 acc[4][2];
   zero(acc);
-  int* my_flag;
-
+  int dtile = -1;  // diagonal tile this task factors after its main work
   if (type == 0) {
-    // ---------------- D(j) ----------------
+    // ---------------- D(0) ----------------
     float4 av[4];
-    load_block(av, tileL(j, j), ld, tr, tc);
-    for (int p = 0; p < j; ++p) {
-      if (!cta_wait(&F[kFlagO + j * 16 + p], ep, a.status)) return;
-      stage_t(Xs, tileL(j, p), ld);
-      __syncthreads();
-      tile_fma(acc, Xs, Xs, tr, tc);
-      __syncthreads();
-    }
-    // S = A - acc (lower part; zeros above the diagonal) into Ys
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int r = 4 * tr + u, c = 4 * tc;
-      float4 o = make_float4(av[u].x - acc[u][0].x, av[u].y - acc[u][0].y,
-                             av[u].z - acc[u][1].x, av[u].w - acc[u][1].y);
-      if (c + 0 > r) o.x = 0.f;
-      if (c + 1 > r) o.y = 0.f;
-      if (c + 2 > r) o.z = 0.f;
-      if (c + 3 > r) o.w = 0.f;
-      *reinterpret_cast<float4*>(Ys + r * kDLD + c) = o;
-    }
+    load_block(av, tileL(0, 0), ld, tr, tc);
+    put_lower(Ys, av, acc, tr, tc);
     __syncthreads();
-    if (tid < 32) {
-      const int f = tile64_potrf<kDLD>(Ys, col, rdiag, tid);
-      if (tid == 0) s_fail = f;
-    }
-    __syncthreads();
-    if (tid < 64) {
-      float t[64];
-      tile64_inverse_column<kDLD>(Ys, rdiag, tid, t);
-#pragma unroll
-      for (int r = 0; r < 64; ++r) Xs[r * kDLD + tid] = t[r];
-    } else {
-      float* dst = tileL(j, j);
-      for (int e = tid - 64; e < 64 * 16; e += kDT - 64) {
-        const int r = e >> 4, c = (e & 15) * 4;
-        *reinterpret_cast<float4*>(dst + r * ld + c) =
-            *reinterpret_cast<const float4*>(Ys + r * kDLD + c);
-      }
-    }
-    __syncthreads();
-    {
-      float* dst = tileV(j, j);
-      for (int e = tid; e < 64 * 16; e += kDT) {
-        const int r = e >> 4, c = (e & 15) * 4;
-        *reinterpret_cast<float4*>(dst + r * ldv + c) =
-            *reinterpret_cast<const float4*>(Xs + r * kDLD + c);
-      }
-    }
-    if (tid == 0 && a.info != nullptr) {
-      const int64_t c0 = a.col0 + int64_t(j) * 64;
-      const int f = s_fail;
-      if (c0 == 0)
-        a.info[mi] = f;
-      else if (f && a.info[mi] == 0)
-        a.info[mi] = int(c0) + f;
-    }
-    my_flag = &F[j];
+    dtile = 0;
   } else if (type == 1) {
-    // ---------------- O(i, j) ----------------
-    float4 av[4];
+    // ---------------- O(i, j) [+ factor of tile (i, i) when i == j + 1] ----------------
+    const bool diag_next = (i == j + 1);
+    float4 av[4], ad[4];
     load_block(av, tileL(i, j), ld, tr, tc);
+    float2 accd[4][2];
+    zero(accd);
+    if (diag_next) {
+      load_block(ad, tileL(i, i), ld, tr, tc);
+      // warm this SM's instruction cache with the factor and inverse (results discarded)
+      put_lower(Ys, ad, accd, tr, tc);
+      __syncthreads();
+      if (tid < 32) warp_factor64(Ys, col, rdiag, tid);
+      __syncthreads();
+      if (tid < 64) inverse_column64(Ys, rdiag, Xs, tid);
+      __syncthreads();
+    }
     for (int p = 0; p < j; ++p) {
       if (!cta_wait(&F[kFlagO + i * 16 + p], ep, a.status)) return;
       if (!cta_wait(&F[kFlagO + j * 16 + p], ep, a.status)) return;
@@ -277,22 +309,20 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
       stage_t(Ys, tileL(j, p), ld);
       __syncthreads();
       tile_fma(acc, Xs, Ys, tr, tc);
+      if (diag_next) tile_fma(accd, Xs, Xs, tr, tc);
       __syncthreads();
     }
-    // C = A - acc, transposed into Xs (Xs[c][r] = C[r][c]) for the solve
+    // C = A - acc, transposed into Xs for the solve X = C T_j^T
     {
-      float cv[4][4];
+      float m[4][4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        cv[u][0] = av[u].x - acc[u][0].x;
-        cv[u][1] = av[u].y - acc[u][0].y;
-        cv[u][2] = av[u].z - acc[u][1].x;
-        cv[u][3] = av[u].w - acc[u][1].y;
+        m[u][0] = av[u].x - acc[u][0].x;
+        m[u][1] = av[u].y - acc[u][0].y;
+        m[u][2] = av[u].z - acc[u][1].x;
+        m[u][3] = av[u].w - acc[u][1].y;
       }
-#pragma unroll
-      for (int v = 0; v < 4; ++v)
-        *reinterpret_cast<float4*>(Xs + (4 * tc + v) * kDLD + 4 * tr) =
-            make_float4(cv[0][v], cv[1][v], cv[2][v], cv[3][v]);
+      put_transposed(Xs, m, tr, tc);
     }
     if (!cta_wait(&F[j], ep, a.status)) return;
     stage_t(Ys, tileV(j, j), ldv);  // Ys[k][c] = T_j[c][k]
@@ -300,7 +330,19 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
     zero(acc);
     tile_fma(acc, Xs, Ys, tr, tc);
     store_block(tileL(i, j), ld, acc, 1.f, tr, tc);
-    my_flag = &F[kFlagO + i * 16 + j];
+    if (!diag_next) {
+      publish(&F[kFlagO + i * 16 + j], ep);
+    } else {
+      __syncthreads();  // Xs and Ys are free
+      float m[4][4];
+      to_array(m, acc);
+      put_transposed(Xs, m, tr, tc);  // Xs[k][r] = L_ij[r][k]
+      publish(&F[kFlagO + i * 16 + j], ep);
+      tile_fma(accd, Xs, Xs, tr, tc);
+      put_lower(Ys, ad, accd, tr, tc);
+      __syncthreads();
+      dtile = i;
+    }
   } else {
     // ---------------- W(i, j) ----------------
     for (int p = j; p < i; ++p) {
@@ -323,14 +365,36 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
     zero(acc);
     tile_fma(acc, Xs, Ys, tr, tc);
     store_block(tileV(i, j), ldv, acc, -1.f, tr, tc);
-    my_flag = &F[kFlagW + i * 16 + j];
+    publish(&F[kFlagW + i * 16 + j], ep);
   }
-  // publish: every thread's stores, then the flag (release at GPU scope)
+  if (dtile < 0) return;
+
+  // ---- diagonal tile d (S in Ys, lower part): factor, T_d = inv(L_dd) into Xs, write
+  // L_dd and T_d, record info, publish D(d) ----
+  const int d = dtile;
+  if (tid < 32) {
+    const int w = warp_factor64(Ys, col, rdiag, tid);
+    if (tid == 0) s_flag[0] = w;
+  }
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    st_release(my_flag, ep);
+  const int f = s_flag[0];
+  if (tid < 64) inverse_column64(Ys, rdiag, Xs, tid);
+  __syncthreads();
+  float* dl = tileL(d, d);
+  float* dv = tileV(d, d);
+  for (int e = tid; e < 64 * 16; e += kDT) {
+    const int r = e >> 4, c = (e & 15) * 4;
+    *reinterpret_cast<float4*>(dl + r * ld + c) = *reinterpret_cast<const float4*>(Ys + r * kDLD + c);
+    *reinterpret_cast<float4*>(dv + r * ldv + c) = *reinterpret_cast<const float4*>(Xs + r * kDLD + c);
   }
+  if (tid == 0 && a.info != nullptr) {
+    const int64_t c0 = a.col0 + int64_t(d) * 64;
+    if (c0 == 0)
+      a.info[mi] = f;
+    else if (f && a.info[mi] == 0)
+      a.info[mi] = int(c0) + f;
+  }
+  publish(&F[d], ep);
 }
 
 }  // namespace
@@ -359,7 +423,7 @@ int launch_diag_block(float* L11, int64_t mstride, int64_t ld, float* V, int64_t
   a.epoch = epoch;
   a.status = device_status_ptr();
   if (a.status == nullptr) return CHOL_ERR_DEVICE;
-  const int64_t ntask = int64_t(nb) * (nb + 1) / 2 + (want_v ? int64_t(nb) * (nb - 1) / 2 : 0);
+  const int64_t ntask = 1 + int64_t(nb) * (nb - 1) / 2 + (want_v ? int64_t(nb) * (nb - 1) / 2 : 0);
   const int64_t ctas = ntask * batch;
   if (ctas > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
   return status_from(launch_pdl(diag_block_kernel, dim3(unsigned(ctas)), dim3(kDT), 0, q, true, a));

@@ -140,9 +140,11 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   CHOL_OPT_CHAIN_SMS: SMs the side-queue update leaves free for the panel chain (24). */
 #define CHOL_OPT_LOOKAHEAD 4
 #define CHOL_OPT_CHAIN_SMS 5
-/*   CHOL_OPT_PANEL_INVERSE: 1 (default) = when n exceeds the outer panel width, the rows
- *   below each panel's diagonal block are solved by one GEMM with the block's inverse;
- *   0 = by the 64-wide left-looking steps over every row of the panel. */
+/*   CHOL_OPT_PANEL_INVERSE: 1 (default) = each outer panel's diagonal block (the whole
+ *   matrix when n <= 1024 and n % 64 == 0) is factored in one launch of 64 x 64 tile
+ *   tasks, and the rows below it are solved by one GEMM with the block's inverse; 2 = the
+ *   same solve, with the block factored by 64-wide kernel steps; 0 = 64-wide left-looking
+ *   steps over every row of the panel. */
 #define CHOL_OPT_PANEL_INVERSE 6
 CHOL_API int chol_set_option(int option, int value);
 

@@ -108,9 +108,23 @@ size_t blocked_inv_bytes(int64_t batch, int64_t n) {
   return size_t(batch) * size_t(NB) * size_t(NB) * sizeof(float) +
          size_t(batch) * kDiagFlags * sizeof(int) + ((size_t(panels) * 4 + 255) & ~size_t(255));
 }
+// n <= outer width (one panel), n % 64 == 0, n <= 1024: the whole matrix is factored by
+// one diagonal-block launch when the batch is small enough for its latency to matter more
+// than throughput: its tile tasks run FP32 FMA at about 10 TFMA/s on a B200, against the
+// tensor-core GEMM chain's ~30 us per 64 columns of latency. batch * n^3 <= kDiagWork is the
+// measured crossover (b64n256: 77 us against 121 us; b640n512: 2.7 ms against 1.48 ms).
+// It needs the 64 x 64 inverse blocks, the tile flags and a ticket counter (zeroed per call).
+constexpr double kDiagWork = 1.2e10;
+size_t blocked_diag_bytes(int64_t batch, int64_t n) {
+  if (n <= 64 || outer_width(n) < n || n % kBlock || n > 16 * kBlock) return 0;
+  if (double(batch) * double(n) * double(n) * double(n) > kDiagWork) return 0;
+  const int64_t nb = n / kBlock;
+  return size_t(batch) * (size_t(nb) * kBlock * kBlock * sizeof(float) + kDiagFlags * sizeof(int)) +
+         256;
+}
 size_t blocked_workspace(int64_t batch, int64_t n) {
   return blocked_workspace_min(batch, n) + blocked_lo_bytes(batch, n) +
-         blocked_inv_bytes(batch, n);
+         blocked_inv_bytes(batch, n) + blocked_diag_bytes(batch, n);
 }
 
 // Tensor-core GEMMs of one call share tensor maps built once over L and the inverse blocks;
@@ -168,6 +182,8 @@ SideQueue* side_queue(int dev) {
   return sq->ok ? sq : nullptr;
 }
 
+// One panel (n <= 1024, n % 64 == 0): the whole matrix goes through diag_block_kernel in one
+// launch (option value 1, the default). Several panels:
 // Panel solve by the inverse of the diagonal block (default; needs the optional workspace):
 // one launch (diag_block_kernel) factors the panel's NB x NB diagonal block and writes
 // V = inv(L11), and the rows below the block are solved by ONE tensor-core GEMM,
@@ -190,6 +206,21 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
   float* V = (lo && inv_bytes && ws_bytes >= min_bytes + lo_bytes + inv_bytes)
                  ? reinterpret_cast<float*>(ws + min_bytes + lo_bytes)
                  : nullptr;
+  const size_t dg_bytes = blocked_diag_bytes(batch, n);
+  if (dg_bytes && g_panel_inverse == 1 && g_gemm_engine != 1 && !use_fused(batch, n) &&
+      ws_bytes >= min_bytes + dg_bytes) {
+    // one panel: the diagonal-block kernel factors the whole matrix in one launch
+    const int nb = int(n / kBlock);
+    float* tblk = reinterpret_cast<float*>(ws + min_bytes);
+    int* fl = reinterpret_cast<int*>(tblk + batch * nb * kBlock * kBlock);
+    unsigned* tk = reinterpret_cast<unsigned*>(fl + batch * kDiagFlags);
+    if (cudaMemsetAsync(fl, 0, size_t(batch) * kDiagFlags * sizeof(int) + 256, q) != cudaSuccess)
+      return CHOL_ERR_LAUNCH;
+    int st = launch_copy_lower(A, L, batch, n, q, true);
+    if (st) return st;
+    return launch_diag_block(L, mstride, n, tblk, int64_t(nb) * kBlock * kBlock, kBlock, nb,
+                             false, fl, tk, 1, info, 0, batch, q);
+  }
   BlockedMaps bm;
   TcMatrixMaps lomap, vmap;
   alignas(64) unsigned char pmap[128];
@@ -399,6 +430,8 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
 
 // Launch count of run_blocked for (batch, n); keep in step with the schedule above.
 int64_t blocked_launches(int64_t batch, int64_t n, bool fused) {
+  if (blocked_diag_bytes(batch, n) && g_panel_inverse == 1 && g_gemm_engine != 1 && !fused)
+    return 2;  // copy_lower + diagonal-block kernel
   const bool pre = blocked_lo_bytes(batch, n) > 0 && g_gemm_engine != 1;
   const bool inv = pre && g_panel_inverse && blocked_inv_bytes(batch, n) > 0;
   const bool diag_kernel = inv && g_panel_inverse == 1;

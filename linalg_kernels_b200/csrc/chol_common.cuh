@@ -158,7 +158,9 @@ int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, i
                        int64_t ld, int64_t batch, int64_t k, int64_t kb, float* Tinv, int* info,
                        cudaStream_t q, bool pdl, int64_t tstride = 4096, int64_t tld = 64);
 // One launch: factor the (64 * nb)-square diagonal block at L11 in place and, with want_v,
-// write V = inv(L11) (lower blocks; the caller zeroes the blocks above the diagonal once).
+// write V = inv(L11) (lower blocks; the caller zeroes the blocks above the diagonal once);
+// without want_v, V (+ m * vstride) only receives the nb inverse diagonal blocks, 64 x 64
+// each, one after another.
 // flags: kDiagFlags ints per matrix and ticket: one counter, both zero before the first
 // launch; epoch: > 0, distinct for every launch that shares the flags (chol_diag.cu).
 constexpr int kDiagFlags = 768;

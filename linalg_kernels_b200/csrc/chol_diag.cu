@@ -44,7 +44,7 @@ constexpr int kFlagO = 256, kFlagW = 512;
 struct DiagArgs {
   float* L;            // (0, 0) of the diagonal block of matrix 0
   int64_t mstride, ld;
-  float* V;            // V = inv(L11), KB x KB per matrix
+  float* V;            // V = inv(L11), KB x KB per matrix (want_v), else nb 64 x 64 T blocks
   int64_t vstride, ldv;
   int* flags;          // kDiagFlags per matrix, zero before the call's first launch
   unsigned* ticket;    // this launch's ticket counter, zero before the launch
@@ -273,6 +273,9 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   const int64_t ld = a.ld, ldv = a.ldv;
   auto tileL = [&](int bi, int bj) { return Lm + int64_t(bi) * 64 * ld + bj * 64; };
   auto tileV = [&](int bi, int bj) { return Vm + int64_t(bi) * 64 * ldv + bj * 64; };
+  // T_d = inv(L_dd): V's diagonal block, or (without V) the d-th 64 x 64 slot of Vm
+  const int64_t ldt = a.want_v ? ldv : 64;
+  auto tileT = [&](int d) { return a.want_v ? tileV(d, d) : Vm + int64_t(d) * 64 * 64; };
   const int tr = tid >> 4, tc = tid & 15;
 
   float2 acc[4][2];
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
       put_transposed(Xs, m, tr, tc);
     }
     if (!cta_wait(&F[j], ep, a.status)) return;
-    stage_t(Ys, tileV(j, j), ldv);  // Ys[k][c] = T_j[c][k]
+    stage_t(Ys, tileT(j), ldt);  // Ys[k][c] = T_j[c][k]
     __syncthreads();
     zero(acc);
     tile_fma(acc, Xs, Ys, tr, tc);
@@ -381,11 +384,11 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   if (tid < 64) inverse_column64(Ys, rdiag, Xs, tid);
   __syncthreads();
   float* dl = tileL(d, d);
-  float* dv = tileV(d, d);
+  float* dv = tileT(d);
   for (int e = tid; e < 64 * 16; e += kDT) {
     const int r = e >> 4, c = (e & 15) * 4;
     *reinterpret_cast<float4*>(dl + r * ld + c) = *reinterpret_cast<const float4*>(Ys + r * kDLD + c);
-    *reinterpret_cast<float4*>(dv + r * ldv + c) = *reinterpret_cast<const float4*>(Xs + r * kDLD + c);
+    *reinterpret_cast<float4*>(dv + r * ldt + c) = *reinterpret_cast<const float4*>(Xs + r * kDLD + c);
   }
   if (tid == 0 && a.info != nullptr) {
     const int64_t c0 = a.col0 + int64_t(d) * 64;
@@ -403,7 +406,8 @@ int launch_diag_block(float* L11, int64_t mstride, int64_t ld, float* V, int64_t
                       int64_t ldv, int nb, bool want_v, int* flags, unsigned* ticket, int epoch,
                       int* info, int64_t col0, int64_t batch, cudaStream_t q) {
   if (nb < 1 || batch <= 0) return CHOL_OK;
-  if (nb > 16 || ld % 4 || ldv % 4 || ldv < 64 * nb || epoch <= 0) return CHOL_ERR_UNSUPPORTED;
+  if (nb > 16 || ld % 4 || ldv % 4 || (want_v && ldv < 64 * nb) || epoch <= 0)
+    return CHOL_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(L11) & 15) || (reinterpret_cast<uintptr_t>(V) & 15))
     return CHOL_ERR_UNSUPPORTED;
   DiagArgs a{};

@@ -244,6 +244,32 @@ def test_multi_panel_sizes(batch, n, lam, panel_inverse, fused):
         lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, -1)
 
 
+# n <= 1024, n % 64 == 0, small batch: the whole matrix in one diagonal-block launch (FP32
+# tile tasks); with the option at 0, the tensor-core chain for the same inputs.
+@pytest.mark.parametrize("batch,n,lam", [(3, 512, 1e4), (2, 1024, 1e5), (5, 640, 1e3),
+                                         (1, 128, 1e2)])
+@pytest.mark.parametrize("panel_inverse", [1, 0])
+def test_single_panel_sizes(batch, n, lam, panel_inverse):
+    lib = _lib.load()
+    lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, panel_inverse)
+    try:
+        a, cond = inputs.spectral(batch, n, lam, 8000 + n, device=DEV)
+        _check_input(a, cond)
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)
+
+
+def test_single_panel_not_spd_info():
+    """info from the one-launch path: the first failing column, as LAPACK reports it."""
+    a, _ = inputs.spectral(4, 256, 10.0, 99, device=DEV)
+    a = a.clone()
+    a[1, 200, 200] = -5.0
+    a[3, 10, 10] = -1.0
+    l, info = cholesky_ex(a)
+    want = torch.linalg.cholesky_ex(a.cpu()).info
+    assert torch.equal(info.cpu(), want), (info.cpu(), want)
+
+
 @pytest.mark.parametrize("n", [2048, 3072])
 def test_lookahead_matches_in_order_schedule(n):
     """The side-queue look-ahead (CHOL_OPT_LOOKAHEAD) only reorders independent work:

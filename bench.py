@@ -5,7 +5,7 @@
     torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU, NCCL)
 
 A *step* is one ``custom_kernel`` call over one (batch, n, n) input. Inputs are
-BASELINE.json's seeded synthetic families (linalg_kernels_b200.inputs), resident in HBM
+the benchmark shapes' seeded synthetic families (linalg_kernels_b200.inputs), resident in HBM
 before timing, taken round-robin from a pool of distinct inputs whose total size exceeds
 twice the 126 MB L2 (no L2 reuse between steps). Timing: W warm-up steps, barrier +
 synchronize, CUDA events around exactly K steps on the launching queue, barrier +
@@ -43,16 +43,20 @@ import torch  # noqa: E402
 DEFAULT_CONFIG = "b1024n64"
 L2_BYTES = 126 * 1024 * 1024
 
-# The reference's published single-B200 times for these shapes,
+# The reference's published single-B200 times for these shapes (references/CURRENT_PERF.md),
 # converted to matrices/s: batch / time.
 REFERENCE_PUBLISHED_S = {
     "b4096n32": 15.7e-6, "b1024n64": 24.1e-6, "b64n256": 191e-6, "b640n512": 2.88e-3,
     "b60n1024": 2.20e-3, "b1n16384": 15.1e-3, "b1n32768": 42.9e-3,
 }
 
-# DRAM bytes (read + write) per launch of the dominant kernel from one ncu capture of the
-# same workload: profiles/<kernel>_<workload>.md (null until captured).
-NCU_TRAFFIC_BYTES: dict[str, float | None] = {}
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of the
+# same workload (python bench.py --ncu-run --config <name>; the short summaries live in the
+# profiles folder). None until captured.
+NCU_TRAFFIC_BYTES: dict[str, float | None] = {
+    "b1024n64": 12.66e6,   # small_potrf_kernel; its writes are still in L2 at kernel end
+    "b4096n32": 16.80e6,   # small_potrf_kernel; likewise
+}
 
 
 def _peaks() -> tuple[dict, str]:
@@ -667,6 +671,25 @@ class _NoDist(Dist):
         self.world, self.rank, self.local, self.pg = 1, 0, 0, None
 
 
+def run_ncu_target(args):
+    """The program the profiles/ ncu captures run: one input of the config (generated on the
+    host for n <= 1024, so the only GPU kernels are ours), warm-up + steps calls of
+    custom_kernel, nothing else (no timing, no baselines)."""
+    from linalg_kernels_b200 import inputs
+    from linalg_kernels_b200.cholesky import custom_kernel
+
+    cfg = inputs.CONFIGS[args.config]
+    dev = torch.device("cuda", 0)
+    gen_dev = "cpu" if cfg.n <= 1024 else dev
+    a, _ = inputs.config_input(cfg, device=gen_dev)
+    a = a.to(dev)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup + args.steps):
+        custom_kernel(a)
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_run": cfg.name, "calls": args.warmup + args.steps}))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -678,14 +701,20 @@ def main(argv=None):
     ap.add_argument("--cpu-budget", type=float, default=10.0,
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--shapes", action=argparse.BooleanOptionalAction, default=True,
-                    help="also time the other BASELINE shapes (N=1 only)")
+                    help="also time the other benchmark shapes (N=1 only)")
     ap.add_argument("--big", action="store_true", help="include b1n32768 in --shapes")
     ap.add_argument("--cyclic", action="store_true",
                     help="b1n32768 through the block-cyclic driver even on one GPU")
     ap.add_argument("--probe", default=None,
                     help="time the tensor-core GEMM alone in the given roles "
                          "(comma list of trailing,inpanel,solve) and exit")
+    ap.add_argument("--ncu-run", action="store_true",
+                    help="only call custom_kernel warmup + steps times on one input of --config "
+                         "(the target of the ncu captures in profiles/)")
     args = ap.parse_args(argv)
+    if args.ncu_run:
+        run_ncu_target(args)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.probe:

@@ -1,6 +1,6 @@
 """Seeded SPD input families for parity tests and benchmarks.
 
-The families are the ones BASELINE.json names for each benchmark shape:
+The families are the ones named for each benchmark shape:
 
 * ``spectral``: A = Q diag(lam) Q^T with Q from the QR of a seeded N(0, 1) matrix and
   lam log-uniform in [1, lam_max], then symmetrised (A + A^T) / 2. cond(A) <= lam_max.
@@ -33,7 +33,7 @@ class Config:
     seed: int
 
 
-# BASELINE.json configs; seeds follow the reference's benchmark seeds (AGENTS.md:74-88).
+# The benchmark configs; seeds follow the reference's benchmark seeds (AGENTS.md:74-88).
 CONFIGS: dict[str, Config] = {c.name: c for c in [
     Config("b4096n32", 4096, 32, "spectral", 1e2, 41032),
     Config("b1024n64", 1024, 64, "spectral", 1e3, 41064),
@@ -94,7 +94,7 @@ def covariance(batch: int, n: int, shift: float, seed: int, device="cpu"):
 
 
 def config_input(cfg: Config | str, device="cpu", batch: int | None = None):
-    """(A, cond) for a named BASELINE config (optionally with a smaller batch)."""
+    """(A, cond) for a named benchmark config (optionally with a smaller batch)."""
     if isinstance(cfg, str):
         cfg = CONFIGS[cfg]
     b = cfg.batch if batch is None else batch

@@ -43,7 +43,7 @@ def load_reference(root: Path):
 def cases():
     """(name, A float32 (b,n,n), cond per matrix) — small, seeded, CPU-generated."""
     out = []
-    # BASELINE.json families at small batch
+    # the benchmark families at small batch
     for b, n, lam, seed in [(8, 32, 1e2, 41032), (4, 64, 1e3, 41064), (1, 256, 1e3, 41256)]:
         a, cond = inputs.spectral(b, n, lam, seed)
         out.append((f"spectral_b{b}n{n}", a, cond))

@@ -3,7 +3,7 @@
 Small cases: elementwise against tests/golden (the reference's own custom_kernel output,
 LAPACK SPOTRF) and against the CPU oracle, with the north-star tolerances
 (||L L^T - A||_F / ||A||_F <= 1e-5, max|L - L_ref| <= cond(A) n eps32 max|L_ref|) plus the
-reference harness's property gate. BASELINE.json sizes: the same bounds against the
+reference harness's property gate. Benchmark sizes: the same bounds against the
 reference path run on the GPU (torch.linalg.cholesky_ex, i.e. submission.py:7 on CUDA)
 and size-independent properties (exact-zero upper, positive diagonal, residual,
 determinism, input untouched).

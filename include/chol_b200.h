@@ -146,6 +146,11 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   same solve, with the block factored by 64-wide kernel steps; 0 = 64-wide left-looking
  *   steps over every row of the panel. */
 #define CHOL_OPT_PANEL_INVERSE 6
+/*   CHOL_OPT_OVERLAP_CALLS: 1 (default) = a call with n <= 64 whose A, L and info are
+ *   disjoint from those of the calls still possibly running on the same queue starts
+ *   loading before they finish (it still completes after them); 0 = every call waits for
+ *   the previous kernel on its queue before reading. */
+#define CHOL_OPT_OVERLAP_CALLS 7
 CHOL_API int chol_set_option(int option, int value);
 
 /*

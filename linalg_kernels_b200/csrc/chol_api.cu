@@ -624,6 +624,11 @@ int chol_set_option(int option, int value) {
     g_chain_sms = value;
     return CHOL_OK;
   }
+  if (option == CHOL_OPT_OVERLAP_CALLS) {
+    if (value < 0 || value > 1) return CHOL_ERR_INVALID_ARG;
+    set_overlap_small(value);
+    return CHOL_OK;
+  }
   if (option == CHOL_OPT_PANEL_INVERSE) {
     if (value < 0 || value > 2) return CHOL_ERR_INVALID_ARG;
     g_panel_inverse = value;

@@ -95,10 +95,15 @@ __device__ __forceinline__ uint64_t pack2(float x, float y) {
 __device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float(uint32_t(v)); }
 __device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
 
+// Every kernel launch on a queue ends the run of back-to-back small calls that may overlap
+// on it (overlap_small_calls in chol_small.cu); the small launcher records its own calls.
+void note_launch(cudaStream_t q);
+
 // Host-side launch helper: cudaLaunchKernelEx with the PDL attribute.
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t q, bool pdl, Args... args) {
+  note_launch(q);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -151,6 +156,8 @@ int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int
 cudaError_t prepare_small();
 int prepare_kernels(int device);
 int launch_small(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q);
+// Overlap of back-to-back independent small calls on one queue (on by default).
+void set_overlap_small(int on);
 int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaStream_t q,
                       bool pdl);
 // Tinv (+ m * tstride, leading dimension tld) receives inv(L_kk) as a 64 x 64 lower triangle.

@@ -53,10 +53,20 @@ constexpr bool small_tma_store() {
 
 // FULL: n == NP and 16-byte aligned rows (vector path). Otherwise scalar loads with
 // identity padding of rows/columns n..NP-1.
+//
+// early: where the kernel takes its programmatic-dependency wait (its grid always completes
+// after its predecessor's), chosen by the host from the buffers of the calls that may still
+// run on the queue (may_start_early):
+//   0  at the start (this call reads what one of them writes, or nothing is known);
+//   1  before the stores (it only writes what one of them reads or writes: the usual case
+//      of back-to-back calls whose output tensors reuse one allocation);
+//   2  at the end (all buffers disjoint).
+// With 1 or 2 a call's loads and pivot chain run under the previous call's factor and stores.
 template <int NP, bool FULL>
 __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 3 : 1)
     small_potrf_kernel(const float* __restrict__ A, float* __restrict__ L, int64_t batch, int n,
-                       int* __restrict__ info, const __grid_constant__ CUtensorMap out_map) {
+                       int* __restrict__ info, const __grid_constant__ CUtensorMap out_map,
+                       int early) {
   constexpr int LPM = SmallShape<NP>::LPM;
   constexpr int R = SmallShape<NP>::R;
   constexpr int MPW = SmallShape<NP>::MPW;
@@ -77,7 +87,7 @@ __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 3 : 1)
   const int64_t mbase = (int64_t(blockIdx.x) * kSmallWarps + warp) * MPW;
   if (FULL) n = NP;
 
-  griddep_wait();
+  if (early == 0) griddep_wait();
   griddep_launch();
 
   // ---- load: lower triangle, coalesced, into this warp's staging tiles ----
@@ -175,6 +185,8 @@ __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 3 : 1)
   }
   __syncwarp();
 
+  if (early == 1) griddep_wait();  // every buffer write below comes after the predecessors
+
   // ---- store. n = 32/64: one tensor store per 32-column half of each matrix from the
   // swizzled tiles; smaller full sizes: one bulk copy per row; otherwise 4-byte stores ----
   if (TMA_OUT) {
@@ -224,6 +236,7 @@ __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 3 : 1)
     const int64_t m = mbase + grp;
     if (m < batch) info[m] = (fail > n) ? 0 : fail;
   }
+  if (early == 2) griddep_wait();
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_small_enc = nullptr;
@@ -286,6 +299,58 @@ bool cached_out_map(CUtensorMap* out, float* L, int64_t batch, int n, int np) {
   return true;
 }
 
+// ---- overlap of back-to-back small calls ----
+// Per (device, queue), the calls that may still be running: a call that took its dependency
+// wait at the start ended the run (everything before it had completed); a call that waits
+// later joins it. Any other kernel launched on the queue clears the run.
+struct Span {
+  uintptr_t lo = 0, hi = 0;
+  bool meets(const Span& o) const { return lo < o.hi && o.lo < hi; }
+};
+struct SmallCall {
+  Span a, l, info;
+};
+struct QueueRun {
+  cudaStream_t q = nullptr;
+  int dev = -1;  // the same handle (the legacy default queue) exists on every device
+  int count = 0;
+  SmallCall calls[8];
+};
+int g_overlap_small = 1;
+std::mutex g_run_mu;
+QueueRun g_runs[16];
+int g_run_next = 0;
+thread_local bool t_in_small_launch = false;
+
+int current_device() {
+  int d = -1;
+  cudaGetDevice(&d);
+  return d;
+}
+
+QueueRun* find_run(cudaStream_t q, int dev) {
+  for (auto& r : g_runs)
+    if (r.count > 0 && r.q == q && r.dev == dev) return &r;
+  return nullptr;
+}
+
+// Where the new call waits (the kernel's `early`): 0 when it reads a buffer that a call of
+// the run writes, 1 when it only writes a buffer that one of them reads or writes, else 2.
+int may_start_early(const QueueRun* run, const SmallCall& c) {
+  if (!g_overlap_small || run == nullptr || run->count == 0 ||
+      run->count >= int(sizeof(run->calls) / sizeof(run->calls[0])))
+    return 0;
+  int level = 2;
+  for (int i = 0; i < run->count; ++i) {
+    const SmallCall& e = run->calls[i];
+    if (c.a.meets(e.l) || c.a.meets(e.info)) return 0;  // read after write
+    if (c.l.meets(e.a) || c.l.meets(e.l) || c.l.meets(e.info) || c.info.meets(e.a) ||
+        c.info.meets(e.l) || c.info.meets(e.info))
+      level = 1;  // write after read / write
+  }
+  return level;
+}
+
 template <int NP>
 int launch_np(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q) {
   constexpr int MPC = kSmallWarps * SmallShape<NP>::MPW;
@@ -299,13 +364,44 @@ int launch_np(const float* A, float* L, int64_t batch, int n, int* info, cudaStr
   if (full && small_tma_store<NP>() && !cached_out_map(&map, L, batch, n, NP))
     return CHOL_ERR_UNSUPPORTED;
   cudaError_t e;
+  SmallCall call;
+  const uintptr_t bytes = uintptr_t(batch) * uintptr_t(n) * uintptr_t(n) * sizeof(float);
+  call.a = {reinterpret_cast<uintptr_t>(A), reinterpret_cast<uintptr_t>(A) + bytes};
+  call.l = {reinterpret_cast<uintptr_t>(L), reinterpret_cast<uintptr_t>(L) + bytes};
+  if (info != nullptr)
+    call.info = {reinterpret_cast<uintptr_t>(info),
+                 reinterpret_cast<uintptr_t>(info) + uintptr_t(batch) * sizeof(int)};
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_run_mu);
+  QueueRun* run = find_run(q, dev);
+  const int early = may_start_early(run, call);
+  t_in_small_launch = true;
   if (full)
     e = launch_pdl(small_potrf_kernel<NP, true>, dim3(unsigned(blocks)), dim3(kSmallWarps * 32),
-                   smem, q, true, A, L, batch, n, info, map);
+                   smem, q, true, A, L, batch, n, info, map, early);
   else
     e = launch_pdl(small_potrf_kernel<NP, false>, dim3(unsigned(blocks)),
-                   dim3(kSmallWarps * 32), smem, q, true, A, L, batch, n, info, map);
-  return status_from(e);
+                   dim3(kSmallWarps * 32), smem, q, true, A, L, batch, n, info, map, early);
+  t_in_small_launch = false;
+  if (e != cudaSuccess) {
+    if (run != nullptr) run->count = 0;
+    return status_from(e);
+  }
+  if (early > 0) {
+    run->calls[run->count++] = call;  // may_start_early needs a run with room
+  } else {
+    // this call waits for everything before it: the run restarts with it
+    QueueRun* r = run;
+    if (r == nullptr) {
+      r = &g_runs[g_run_next];
+      g_run_next = (g_run_next + 1) % int(sizeof(g_runs) / sizeof(g_runs[0]));
+    }
+    r->q = q;
+    r->dev = dev;
+    r->count = 0;
+    r->calls[r->count++] = call;
+  }
+  return CHOL_OK;
 }
 
 template <int NP>
@@ -328,6 +424,22 @@ cudaError_t prepare_small() {
   if ((e = set_smem_np<16>()) != cudaSuccess) return e;
   if ((e = set_smem_np<32>()) != cudaSuccess) return e;
   return set_smem_np<64>();
+}
+
+// Called by launch_pdl before every kernel launch: the queue's run of small calls ends
+// (the small launcher updates the run itself around its own launch).
+void note_launch(cudaStream_t q) {
+  if (t_in_small_launch) return;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_run_mu);
+  for (auto& r : g_runs)
+    if (r.q == q && r.dev == dev) r.count = 0;
+}
+
+void set_overlap_small(int on) {
+  std::lock_guard<std::mutex> lock(g_run_mu);
+  g_overlap_small = on;
+  for (auto& r : g_runs) r.count = 0;
 }
 
 int launch_small(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q) {

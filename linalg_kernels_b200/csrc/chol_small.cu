@@ -22,7 +22,17 @@ namespace chol {
 
 namespace {
 
-constexpr int kSmallWarps = 4;
+// Warps per CTA and the CTAs per SM the launch bounds ask for. n = 64 uses 2-warp CTAs
+// (72 KB of staging each, 2-3 per SM): back-to-back calls then find room on every SM for
+// the next call's CTAs (9.8 us per call at b=1024 against 10.9 us with 4-warp CTAs).
+template <int NP>
+constexpr int small_warps() {
+  return NP >= 64 ? 2 : 4;
+}
+template <int NP>
+constexpr int small_min_ctas() {
+  return NP <= 32 ? 3 : 2;
+}
 
 // Lanes per matrix for each padded size: 8 lanes x 4 rows for n <= 32 (four matrices per
 // warp share each per-column step), a full warp x 2 rows for n = 64.
@@ -42,7 +52,7 @@ constexpr int small_tile_floats() {
 }
 template <int NP>
 constexpr size_t small_smem_bytes() {
-  return size_t(kSmallWarps) * SmallShape<NP>::MPW *
+  return size_t(small_warps<NP>()) * SmallShape<NP>::MPW *
              (size_t(small_tile_floats<NP>()) + SmallShape<NP>::COLS) * 4 + 1024;
 }
 // The tensor-store path covers n = 32 and n = 64 (rows of 128-byte multiples).
@@ -63,7 +73,7 @@ constexpr bool small_tma_store() {
 //   2  at the end (all buffers disjoint).
 // With 1 or 2 a call's loads and pivot chain run under the previous call's factor and stores.
 template <int NP, bool FULL>
-__global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 3 : 1)
+__global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
     small_potrf_kernel(const float* __restrict__ A, float* __restrict__ L, int64_t batch, int n,
                        int* __restrict__ info, const __grid_constant__ CUtensorMap out_map,
                        int early) {
@@ -82,9 +92,9 @@ __global__ void __launch_bounds__(kSmallWarps * 32, NP <= 32 ? 3 : 1)
   const int grp = lane / LPM;
   const int gl = lane % LPM;
   float* stage = smem + size_t(warp) * MPW * TILE;
-  float* col = smem + size_t(kSmallWarps) * MPW * TILE +
+  float* col = smem + size_t(small_warps<NP>()) * MPW * TILE +
                size_t(warp * MPW + grp) * SmallShape<NP>::COLS;
-  const int64_t mbase = (int64_t(blockIdx.x) * kSmallWarps + warp) * MPW;
+  const int64_t mbase = (int64_t(blockIdx.x) * small_warps<NP>() + warp) * MPW;
   if (FULL) n = NP;
 
   if (early == 0) griddep_wait();
@@ -353,7 +363,7 @@ int may_start_early(const QueueRun* run, const SmallCall& c) {
 
 template <int NP>
 int launch_np(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q) {
-  constexpr int MPC = kSmallWarps * SmallShape<NP>::MPW;
+  constexpr int MPC = small_warps<NP>() * SmallShape<NP>::MPW;
   const int64_t blocks = (batch + MPC - 1) / MPC;
   if (blocks > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
   const size_t smem = small_smem_bytes<NP>();
@@ -377,11 +387,11 @@ int launch_np(const float* A, float* L, int64_t batch, int n, int* info, cudaStr
   const int early = may_start_early(run, call);
   t_in_small_launch = true;
   if (full)
-    e = launch_pdl(small_potrf_kernel<NP, true>, dim3(unsigned(blocks)), dim3(kSmallWarps * 32),
+    e = launch_pdl(small_potrf_kernel<NP, true>, dim3(unsigned(blocks)), dim3(small_warps<NP>() * 32),
                    smem, q, true, A, L, batch, n, info, map, early);
   else
     e = launch_pdl(small_potrf_kernel<NP, false>, dim3(unsigned(blocks)),
-                   dim3(kSmallWarps * 32), smem, q, true, A, L, batch, n, info, map, early);
+                   dim3(small_warps<NP>() * 32), smem, q, true, A, L, batch, n, info, map, early);
   t_in_small_launch = false;
   if (e != cudaSuccess) {
     if (run != nullptr) run->count = 0;

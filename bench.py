@@ -411,8 +411,17 @@ def _kernel_ms_graph(lib, pool, dev, b, n, reps=20):
 def _roofline(args, cfg, per_step_ms, peaks, peak_kind, lib, pool, dev, dist):
     n, b = cfg.n, cfg.batch
     if n <= 256 and int(lib.chol_launch_count(b, n)) == 1:
-        # single launch per call: that kernel's duration from back-to-back graph replay
+        # single launch per call: launches per second of back-to-back graph replay. Launches
+        # of consecutive calls overlap (CHOL_OPT_OVERLAP_CALLS), so this is the steady-state
+        # interval per launch; the isolated launch (overlap off) is reported beside it.
+        from linalg_kernels_b200 import _lib
+
         t = dist.max(_kernel_ms_graph(lib, pool, dev, b, n)) / 1e3
+        lib.chol_set_option(_lib.CHOL_OPT_OVERLAP_CALLS, 0)
+        try:
+            t_iso = dist.max(_kernel_ms_graph(lib, pool, dev, b, n)) / 1e3
+        finally:
+            lib.chol_set_option(_lib.CHOL_OPT_OVERLAP_CALLS, 1)
         bytes_ = 8.0 * n * n * b
         achieved = bytes_ / t / 1e9
         peak = peaks["hbm_gbs"]
@@ -421,7 +430,11 @@ def _roofline(args, cfg, per_step_ms, peaks, peak_kind, lib, pool, dev, dist):
                 "peak_kind": f"{peak_kind} hbm_gbs (burst copy)",
                 "traffic": NCU_TRAFFIC_BYTES.get(cfg.name),
                 "algorithmic_bytes_per_launch": bytes_, "launch_ms": t * 1e3,
-                "timing": "CUDA graph of 20 back-to-back calls, events around the replay"}
+                "isolated_launch_ms": t_iso * 1e3,
+                "isolated_frac": bytes_ / t_iso / 1e9 / peak,
+                "timing": "CUDA graph of 20 back-to-back calls, events around the replay; "
+                          "launch_ms = replay time / 20 with consecutive launches overlapping, "
+                          "isolated_launch_ms = the same with the overlap off"}
     # blocked path: time the largest trailing update launch alone (its own CUDA events)
     return _gemm_roofline(cfg, peaks, peak_kind, lib, pool, dev, dist)
 

@@ -198,10 +198,13 @@ CHOL_API int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t 
                      int64_t diag_offset, int lower_only, void* queue);
 
 /* Factor a tall panel in place: the first w columns of an m-row row-major view (leading
-   dimension ld) whose element (0, 0) sits on the matrix diagonal, left-looking in 64-wide
-   steps (diagonal block + inverse, solve of the rows below). Tinv: 64*64 floats of device
-   workspace. info (nullable, one int): first failing column of the panel (1-based) or 0.
-   The per-panel step of the multi-GPU block-column-cyclic driver. */
+   dimension ld) whose element (0, 0) sits on the matrix diagonal. With w a multiple of 64
+   (<= 1024) and 16-byte aligned rows: the w x w top block and its inverse in one launch,
+   then one GEMM solves every row below (scratch cached by the library per device, grown
+   with cudaMalloc on first need); otherwise left-looking 64-wide steps (diagonal block +
+   inverse, solve of the rows below). Tinv: 64*64 floats of device workspace (used by the
+   64-wide steps). info (nullable, one int): first failing column of the panel (1-based) or
+   0. The per-panel step of the multi-GPU block-column-cyclic driver. */
 CHOL_API int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv,
                                   int* info, void* queue);
 

@@ -116,3 +116,46 @@ def test_cyclic_gemm_matches_per_block(world, nblk):
         want[r:, b * bs:b * bs + w] = torch.where(keep, upd, want[r:, b * bs:b * bs + w])
     err = (c.double() - want).abs().max().item()
     assert err < 8 * k * 2.0 ** -22 * 25.0, err
+
+
+@pytest.mark.parametrize("m,w", [(3000, 256), (1500, 128), (256, 256), (900, 100)])
+@pytest.mark.parametrize("panel_inverse", [1, 0])
+def test_panel_potrf_building_block(m, w, panel_inverse):
+    """chol_panel_potrf_f32: the first w columns of an m-row panel factored in place equal
+    the first w columns of an FP64 Cholesky of the m x m matrix (the panel's rows), with
+    the one-launch block + inverse solve (option 1, w % 64 == 0) and the 64-wide steps."""
+    from linalg_kernels_b200 import _lib
+    from linalg_kernels_b200.distributed import CudaOps
+
+    lib = _lib.load()
+    a, _ = inputs.covariance(1, m, 0.5, 31 * m + w)
+    full = a[0].to(DEV)
+    panel = torch.tril(full).contiguous()  # the panel is the first w columns of these rows
+    tinv = torch.empty(64, 64, device=DEV)
+    info = torch.full((1,), -1, dtype=torch.int32, device=DEV)
+    lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, panel_inverse)
+    try:
+        CudaOps(torch.device(DEV)).panel_potrf(panel[:, :w], tinv, info)
+        torch.cuda.synchronize()
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)
+    want = torch.linalg.cholesky(full.double())[:, :w]
+    got = torch.tril(panel[:, :w].double())
+    err = (got - want).abs().max().item() / want.abs().max().item()
+    assert int(info.item()) == 0
+    assert err < 2e-5, err
+
+
+def test_panel_potrf_reports_not_spd():
+    from linalg_kernels_b200.distributed import CudaOps
+
+    m, w = 1024, 256
+    a, _ = inputs.covariance(1, m, 0.5, 5)
+    full = a[0].clone()
+    full[130, 130] = -50.0
+    panel = torch.tril(full).to(DEV).contiguous()
+    tinv = torch.empty(64, 64, device=DEV)
+    info = torch.full((1,), -1, dtype=torch.int32, device=DEV)
+    CudaOps(torch.device(DEV)).panel_potrf(panel[:, :w], tinv, info)
+    torch.cuda.synchronize()
+    assert int(info.item()) == 131

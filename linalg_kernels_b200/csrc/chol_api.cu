@@ -482,6 +482,67 @@ int potrf_impl(const float* A, float* L, int64_t batch, int64_t n, int* info, vo
   return run_blocked(A, L, batch, n, info, static_cast<float*>(ws), ws_bytes, q);
 }
 
+// Scratch of the panel factor by the block inverse (V, tile flags, ticket, the solved rows),
+// cached per device and grown on demand, like the workspace of chol_potrf_batched_f32.
+struct PanelScratch {
+  std::mutex mu;
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+void* cached_scratch(PanelScratch& s, size_t need) {
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (s.bytes < need) {
+    if (s.p != nullptr) cudaFree(s.p);
+    s.p = nullptr;
+    s.bytes = 0;
+    if (cudaMalloc(&s.p, need) != cudaSuccess) return nullptr;
+    s.bytes = need;
+  }
+  return s.p;
+}
+
+void* panel_scratch(int dev, size_t need) {
+  static PanelScratch ps[64];
+  if (dev < 0 || dev >= 64) return nullptr;
+  return cached_scratch(ps[dev], need);
+}
+
+// Panel of width w (w % 64 == 0, w <= 1024): diag_block_kernel factors the w x w top block
+// and writes V = inv(L11); one GEMM solves every row below, X = A21 V^T, into scratch;
+// tf32_lo_kernel copies X back into L (its low-part output stays in scratch, unused).
+int panel_potrf_inverse(float* L, int64_t ld, int64_t m, int64_t w, int* info, int dev,
+                        cudaStream_t q) {
+  const int nb = int(w / kBlock);
+  const size_t vbytes = size_t(w) * size_t(w) * sizeof(float);
+  const size_t fbytes = kDiagFlags * sizeof(int) + 256;
+  const size_t xbytes = size_t(m - w) * size_t(w) * sizeof(float);
+  char* base = static_cast<char*>(panel_scratch(dev, vbytes + fbytes + xbytes));
+  if (base == nullptr) return CHOL_ERR_WORKSPACE;
+  float* V = reinterpret_cast<float*>(base);
+  int* flags = reinterpret_cast<int*>(base + vbytes);
+  unsigned* ticket = reinterpret_cast<unsigned*>(flags + kDiagFlags);
+  float* X = reinterpret_cast<float*>(base + vbytes + fbytes);
+  if (cudaMemsetAsync(V, 0, vbytes + fbytes, q) != cudaSuccess) return CHOL_ERR_LAUNCH;
+  int st = launch_diag_block(L, 0, ld, V, 0, w, nb, m > w, flags, ticket, 1, info, 0, 1, q);
+  if (st || m == w) return st;
+  GemmArgs x{};
+  x.C = X;
+  x.ldc = w;
+  x.P = L + w * ld;
+  x.ldp = ld;
+  x.Q = V;
+  x.ldq = w;
+  x.m = m - w;
+  x.ncols = w;
+  x.K = w;
+  x.alpha = 1.f;
+  x.beta = 0.f;
+  x.batch = 1;
+  if ((st = launch_gemm(x, q, true))) return st;
+  return launch_tf32_lo(X, w, X, w, m - w, w, 1, 0, 0, q, L + w * ld, ld, 0);
+}
+
 }  // namespace
 
 int prepare_device_checked(int dev) { return prepare_device(dev); }
@@ -715,64 +776,6 @@ int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t ldc, int6
   return launch_gemm(g, static_cast<cudaStream_t>(queue), true);
 }
 
-// Scratch of the panel factor by the block inverse (V, tile flags, ticket, the solved rows),
-// cached per device and grown on demand, like the workspace of chol_potrf_batched_f32.
-struct PanelScratch {
-  std::mutex mu;
-  void* p = nullptr;
-  size_t bytes = 0;
-};
-
-void* panel_scratch(int dev, size_t need) {
-  static PanelScratch ps[64];
-  if (dev < 0 || dev >= 64) return nullptr;
-  PanelScratch& s = ps[dev];
-  std::lock_guard<std::mutex> lock(s.mu);
-  if (s.bytes < need) {
-    if (s.p != nullptr) cudaFree(s.p);
-    s.p = nullptr;
-    s.bytes = 0;
-    if (cudaMalloc(&s.p, need) != cudaSuccess) return nullptr;
-    s.bytes = need;
-  }
-  return s.p;
-}
-
-// Panel of width w (w % 64 == 0, w <= 1024): diag_block_kernel factors the w x w top block
-// and writes V = inv(L11); one GEMM solves every row below, X = A21 V^T, into scratch;
-// tf32_lo_kernel copies X back into L (its low-part output stays in scratch, unused).
-int panel_potrf_inverse(float* L, int64_t ld, int64_t m, int64_t w, int* info, int dev,
-                        cudaStream_t q) {
-  const int nb = int(w / kBlock);
-  const size_t vbytes = size_t(w) * size_t(w) * sizeof(float);
-  const size_t fbytes = kDiagFlags * sizeof(int) + 256;
-  const size_t xbytes = size_t(m - w) * size_t(w) * sizeof(float);
-  char* base = static_cast<char*>(panel_scratch(dev, vbytes + fbytes + xbytes));
-  if (base == nullptr) return CHOL_ERR_WORKSPACE;
-  float* V = reinterpret_cast<float*>(base);
-  int* flags = reinterpret_cast<int*>(base + vbytes);
-  unsigned* ticket = reinterpret_cast<unsigned*>(flags + kDiagFlags);
-  float* X = reinterpret_cast<float*>(base + vbytes + fbytes);
-  if (cudaMemsetAsync(V, 0, vbytes + fbytes, q) != cudaSuccess) return CHOL_ERR_LAUNCH;
-  int st = launch_diag_block(L, 0, ld, V, 0, w, nb, m > w, flags, ticket, 1, info, 0, 1, q);
-  if (st || m == w) return st;
-  GemmArgs x{};
-  x.C = X;
-  x.ldc = w;
-  x.P = L + w * ld;
-  x.ldp = ld;
-  x.Q = V;
-  x.ldq = w;
-  x.m = m - w;
-  x.ncols = w;
-  x.K = w;
-  x.alpha = 1.f;
-  x.beta = 0.f;
-  x.batch = 1;
-  if ((st = launch_gemm(x, q, true))) return st;
-  return launch_tf32_lo(X, w, X, w, m - w, w, 1, 0, 0, q, L + w * ld, ld, 0);
-}
-
 int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv, int* info,
                          void* queue) {
   if (L == nullptr || Tinv == nullptr || m < 0 || w < 0 || w > m || ld < w)
@@ -855,7 +858,21 @@ int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t ncols, int
   g.cmap_block = col_block;
   g.cmap_stride = col_stride;
   if (!tc_supported(g)) return CHOL_ERR_UNSUPPORTED;
-  return launch_gemm_tc(g, static_cast<cudaStream_t>(queue), true, nullptr);
+  cudaStream_t q = static_cast<cudaStream_t>(queue);
+  if (P == Q && ldp == ldq && K % 4 == 0 && g_gemm_engine != 1) {
+    // low TF32 parts of the panel once (cached scratch), then the GEMM loads them with TMA
+    // instead of splitting every tile in shared memory
+    static PanelScratch lo_cache[64];
+    float* lo = dev < 64 ? static_cast<float*>(cached_scratch(lo_cache[dev],
+                                                              size_t(m) * size_t(K) * 4))
+                         : nullptr;
+    if (lo != nullptr) {
+      if ((st = launch_tf32_lo(P, ldp, lo, K, m, K, 1, 0, 0, q))) return st;
+      st = launch_gemm_tc_prelo(g, lo, K, q, true);
+      if (st != CHOL_ERR_UNSUPPORTED) return st;
+    }
+  }
+  return launch_gemm_tc(g, q, true, nullptr);
 }
 
 }  // extern "C"

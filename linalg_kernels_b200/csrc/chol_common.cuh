@@ -205,6 +205,10 @@ int launch_tf32_lo(const float* src, int64_t lds, float* dst, int64_t ldd, int64
                    int64_t cols, int64_t batch, int64_t sstride, int64_t dstride, cudaStream_t q,
                    float* copy = nullptr, int64_t ldcopy = 0, int64_t cstride = 0);
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t q, bool pdl, int* status);
+// P == Q with their TF32 low parts precomputed in lo (same rows, leading dimension ldlo);
+// BN = 256, column-cyclic map allowed.
+int launch_gemm_tc_prelo(const GemmArgs& g, const float* lo, int64_t ldlo, cudaStream_t q,
+                         bool pdl);
 cudaError_t prepare_tc();
 int read_and_clear_status(int* out);
 // Device address of the status word (for kernels in other translation units).

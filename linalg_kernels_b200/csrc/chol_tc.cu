@@ -492,6 +492,29 @@ int launch_tc_bn(const GemmArgs& g, cudaStream_t q, bool pdl, int* status) {
 
 }  // namespace
 
+// Per-launch maps with precomputed low parts: P = Q (the same rows; Q's rows follow the
+// column-cyclic map), lo = the TF32 low parts of P (same rows, leading dimension ldlo).
+int launch_gemm_tc_prelo(const GemmArgs& g, const float* lo, int64_t ldlo, cudaStream_t q,
+                         bool pdl) {
+  constexpr int BN = 256;
+  if (g.P != g.Q || g.ldp != g.ldq || g.batch != 1) return CHOL_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(lo) & 15) || ldlo % 4) return CHOL_ERR_UNSUPPORTED;
+  if (g.cmap_block && (g.cmap_block != 256 || g.cmap_stride < 256 || g.cmap_stride % 256))
+    return CHOL_ERR_UNSUPPORTED;
+  const int64_t qrows = g.cmap_block ? (g.ncols - 1) + ((g.ncols - 1) / g.cmap_block) *
+                                                          (g.cmap_stride - g.cmap_block) + 1
+                                     : g.ncols;
+  if (qrows > g.m) return CHOL_ERR_UNSUPPORTED;  // Q's rows are rows of P
+  CUtensorMap mp, mq, mplo, mqlo;
+  if (!make_map(&mp, g.P, g.K, g.m, 1, g.ldp, 0, kBM) ||
+      !make_map(&mq, g.Q, g.K, qrows, 1, g.ldq, 0, BN) ||
+      !make_map(&mplo, lo, g.K, g.m, 1, ldlo, 0, kBM) ||
+      !make_map(&mqlo, lo, g.K, qrows, 1, ldlo, 0, BN))
+    return CHOL_ERR_UNSUPPORTED;
+  return launch_tc_maps<BN>(g, mp, mq, TmaOrigin{0, 0, 0, 0, 0, 0}, q, pdl, nullptr, &mplo,
+                            &mqlo);
+}
+
 bool tc_supported(const GemmArgs& g) {
   if (!resolve_encode()) return false;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };

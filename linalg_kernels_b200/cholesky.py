@@ -58,6 +58,7 @@ def workspace_bytes(batch: int, n: int) -> int:
 
 
 _ws_bytes: dict[tuple[int, int], int] = {}
+_one_device: bool | None = None  # a single visible GPU: no device switch is ever needed
 
 
 def _workspace_bytes(lib, batch: int, n: int) -> int:
@@ -78,8 +79,11 @@ def _factor(data: torch.Tensor, want_info: bool):
         else None
     if batch == 0 or n == 0:
         return out, info
+    global _one_device
+    if _one_device is None:
+        _one_device = torch.cuda.device_count() == 1
     dev = data.device.index
-    if dev != torch.cuda.current_device():
+    if not _one_device and dev != torch.cuda.current_device():
         with torch.cuda.device(dev):
             return _launch(lib, data, out, info, batch, n, dev)
     return _launch(lib, data, out, info, batch, n, dev)

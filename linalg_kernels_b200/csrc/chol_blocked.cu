@@ -66,7 +66,7 @@ int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaSt
 }
 
 // =====================================================================================
-// potrf_block: one CTA (128 threads) per matrix factors the kb x kb block at (k, k).
+// potrf_block: one CTA per matrix factors the kb x kb block at (k, k).
 //   S (+ m*sstride) with leading dimension lds is where the block is read from (A for the
 //   first block when the copy is fused, else L); the factor goes to L (+ m*stride, ld).
 //   Strict upper part of the block is written as zeros.
@@ -77,7 +77,11 @@ int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaSt
 constexpr int kPB = 64;         // block size handled by one CTA
 constexpr int kPBLD = kPB + 4;  // smem row stride
 
-__global__ void __launch_bounds__(128)
+// NT = 128: threads 64..127 write the factored block while 0..63 compute the inverse (the
+// shortest CTA; 3 per SM). NT = 64: two warps do both in turn (6 CTAs per SM): for batches
+// beyond one wave of 128-thread CTAs (b640n512: 30 -> ~15 us per launch).
+template <int NT>
+__global__ void __launch_bounds__(NT)
     potrf_block_kernel(const float* __restrict__ S, int64_t sstride, int64_t lds,
                        float* __restrict__ L, int64_t stride, int64_t ld, int64_t k, int kb,
                        float* __restrict__ Tinv, int64_t tstride, int64_t tld,
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(128)
 
   // load the block: every 4-byte element of the lower part in flight at once (cp.async),
   // identity outside kb, zeros above the diagonal
-  for (int idx = tid; idx < kPB * kPB; idx += 128) {
+  for (int idx = tid; idx < kPB * kPB; idx += NT) {
     const int r = idx / kPB, c = idx % kPB;
     if (r < kb && c < kb) {
       if (c <= r)
@@ -121,20 +125,22 @@ __global__ void __launch_bounds__(128)
   }
   __syncthreads();
 
-  if (tid >= 64) {
-    // threads 64..127: write the factored block (rows/cols < kb) to L
-    for (int idx = tid - 64; idx < kb * kb; idx += 64) {
-      const int r = idx / kb, c = idx - r * kb;
-      dst[r * ld + c] = tile[r * kPBLD + c];
-    }
-  } else if (Tinv != nullptr) {
-    // threads 0..63: column c of T = inv(L_kk)
+  // T = inv(L_kk): thread c (< 64) computes column c in registers and writes it out
+  if (Tinv != nullptr && tid < 64) {
     const int c = tid;
     float t[kPB];
     tile64_inverse_column<kPBLD>(tile, rdiag, c, t);
     float* tp = Tinv + m * tstride;
 #pragma unroll
     for (int i = 0; i < kPB; ++i) tp[i * tld + c] = t[i];
+  }
+  // the factored block (rows/cols < kb) to L: threads 64..127, or all threads after T
+  const int w0 = NT > 64 ? 64 : 0;
+  if (tid >= w0) {
+    for (int idx = tid - w0; idx < kb * kb; idx += NT - w0) {
+      const int r = idx / kb, c = idx - r * kb;
+      dst[r * ld + c] = tile[r * kPBLD + c];
+    }
   }
 }
 
@@ -143,8 +149,15 @@ int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, i
                        cudaStream_t q, bool pdl, int64_t tstride, int64_t tld) {
   if (kb < 1 || kb > kPB || tld < kPB) return CHOL_ERR_UNSUPPORTED;
   if (batch > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
-  cudaError_t e = launch_pdl(potrf_block_kernel, dim3(unsigned(batch)), dim3(128), 0, q, pdl, S,
-                             sstride, lds, L, stride, ld, k, int(kb), Tinv, tstride, tld, info);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e =
+      batch > int64_t(sms) * 3
+          ? launch_pdl(potrf_block_kernel<64>, dim3(unsigned(batch)), dim3(64), 0, q, pdl, S,
+                       sstride, lds, L, stride, ld, k, int(kb), Tinv, tstride, tld, info)
+          : launch_pdl(potrf_block_kernel<128>, dim3(unsigned(batch)), dim3(128), 0, q, pdl, S,
+                       sstride, lds, L, stride, ld, k, int(kb), Tinv, tstride, tld, info);
   return status_from(e);
 }
 

@@ -132,7 +132,7 @@ size_t blocked_workspace(int64_t batch, int64_t n) {
 // built (unaligned rows) or the engine option asks for it.
 struct BlockedMaps {
   bool ok = false;
-  TcMatrixMaps L, T;
+  TcMatrixMaps L, T, A;  // A: only for the one-panel chain that reads the input directly
 };
 
 int gemm_on(const GemmArgs& g, const BlockedMaps& bm, const TcMatrixMaps& pm,
@@ -248,7 +248,14 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
   const bool fused = bm.ok && use_fused(batch, n);
   if (fused && cudaMemsetAsync(counters, 0, size_t(batch) * sizeof(unsigned), q) != cudaSuccess)
     return CHOL_ERR_LAUNCH;
-  int st = launch_copy_lower(A, L, batch, n, q, true);
+  // One panel (n <= outer width), 64-wide chain: every block column of L is produced once,
+  // so the chain reads A where the copy would be read: the first diagonal block and solve
+  // take A, each left-looking update takes its beta * C term from A and writes L, and only
+  // the part of L right of the diagonal blocks needs zeros (a third of copy_lower's traffic).
+  const bool from_a = NBw >= n && !fused &&
+                      (!bm.ok || tc_make_matrix_maps(A, n, n, n, batch, mstride, &bm.A));
+  int st = from_a ? launch_zero_upper(L, batch, n, q, true)
+                  : launch_copy_lower(A, L, batch, n, q, true);
   if (st) return st;
   // the previous panel's side-queue update must finish before the panel buffer is rewritten
   auto join_pending = [&]() -> int {
@@ -288,6 +295,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
         // panel's already factored columns [K0, k) in one GEMM (K = k - K0)
         GemmArgs u{};
         u.C = L + k * n + k;
+        if (from_a) u.Csrc = A + k * n + k;
         u.cstride = mstride;
         u.ldc = n;
         u.P = L + k * n + K0;
@@ -307,7 +315,10 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
         st = gemm_on(u, bm, bm.L, bm.L, q, chain_cap);
         if (st) return st;
       }
-      st = launch_potrf_block(L, mstride, n, L, mstride, n, batch, k, kb, Tk, info, q, true,
+      // (from_a: block column 0 is read from A, the others after their left update in L)
+      const bool first_from_a = from_a && k == 0;
+      st = launch_potrf_block(first_from_a ? A : L, mstride, n, L, mstride, n, batch, k, kb, Tk,
+                              info, q, true,
                               tstride, tld);
       if (st) return st;
       const int64_t below = chain_end - k - kb;
@@ -317,7 +328,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       s.C = L + (k + kb) * n + k;
       s.cstride = mstride;
       s.ldc = n;
-      s.P = s.C;
+      s.P = first_from_a ? A + (k + kb) * n + k : s.C;
       s.pstride = mstride;
       s.ldp = n;
       s.Q = Tk;
@@ -330,7 +341,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       s.beta = 0.f;
       s.lower_only = 0;
       s.batch = batch;
-      st = gemm_on(s, bm, bm.L, inv ? vmap : bm.T, q, chain_cap);
+      st = gemm_on(s, bm, first_from_a ? bm.A : bm.L, inv ? vmap : bm.T, q, chain_cap);
       if (st) return st;
     }
     if (rest <= 0) continue;

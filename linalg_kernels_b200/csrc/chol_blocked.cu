@@ -66,6 +66,48 @@ int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaSt
 }
 
 // =====================================================================================
+// zero_upper: L[m][i][j] = 0 for j >= 64 * (i / 64 + 1), the part of the strict upper
+// triangle right of each row's 64-wide diagonal block (the diagonal blocks themselves are
+// written whole, zeros included, by potrf_block). Replaces copy_lower when the schedule
+// reads A directly. One thread per 4 consecutive elements (vector path when n % 4 == 0).
+// =====================================================================================
+template <bool VEC>
+__global__ void __launch_bounds__(256) zero_upper_kernel(float* __restrict__ L, int64_t batch,
+                                                         int64_t n) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t per_row = VEC ? n / 4 : n;
+  const int64_t total = batch * n * per_row;
+  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t row_g = t / per_row;
+    const int64_t c = (t - row_g * per_row) * (VEC ? 4 : 1);
+    const int64_t i = row_g % n;
+    if (c < (i / 64 + 1) * 64) continue;
+    if (VEC)
+      *reinterpret_cast<float4*>(L + row_g * n + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    else
+      L[row_g * n + c] = 0.f;
+  }
+}
+
+int launch_zero_upper(float* L, int64_t batch, int64_t n, cudaStream_t q, bool pdl) {
+  const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(L) & 15) == 0);
+  const int64_t work = batch * n * (vec ? n / 4 : n);
+  int64_t blocks = (work + 255) / 256;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (blocks > int64_t(sms) * 16) blocks = int64_t(sms) * 16;
+  if (blocks < 1) blocks = 1;
+  cudaError_t e = vec ? launch_pdl(zero_upper_kernel<true>, dim3(unsigned(blocks)), dim3(256), 0,
+                                   q, pdl, L, batch, n)
+                      : launch_pdl(zero_upper_kernel<false>, dim3(unsigned(blocks)), dim3(256),
+                                   0, q, pdl, L, batch, n);
+  return status_from(e);
+}
+
+// =====================================================================================
 // potrf_block: one CTA per matrix factors the kb x kb block at (k, k).
 //   S (+ m*sstride) with leading dimension lds is where the block is read from (A for the
 //   first block when the copy is fused, else L); the factor goes to L (+ m*stride, ld).
@@ -441,13 +483,14 @@ __global__ void __launch_bounds__(BN * 2)
     const int64_t r = r0 + ty * TM + i;
     if (r >= g.m) continue;
     float* crow = C + r * g.ldc;
+    const float* srow = (g.Csrc != nullptr ? g.Csrc + mi * g.cstride : C) + r * g.ldc;
 #pragma unroll
     for (int j = 0; j < TN; ++j) {
       const int64_t c = c0 + tx * TN + j;
       if (c >= g.ncols) continue;
       if (g.lower_only && c > r + g.diag_offset) continue;
       float v = g.alpha * acc[i][j];
-      if (g.beta != 0.f) v = fmaf(g.beta, crow[c], v);
+      if (g.beta != 0.f) v = fmaf(g.beta, srow[c], v);
       crow[c] = v;
     }
   }

@@ -141,6 +141,9 @@ struct GemmArgs {
   // i.e. consecutive local blocks of cmap_block columns are cmap_stride global columns
   // apart; lower_only compares global columns with rows. Q's rows follow the same map.
   int64_t cmap_block, cmap_stride;
+  // Optional source of the beta * C term (same layout as C): C = alpha P Q^T + beta Csrc.
+  // nullptr: C itself (read-modify-write).
+  const float* Csrc;
 };
 
 // Entry-point plumbing shared by the C-ABI files (chol_api.cu).
@@ -160,6 +163,8 @@ int launch_small(const float* A, float* L, int64_t batch, int n, int* info, cuda
 void set_overlap_small(int on);
 int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaStream_t q,
                       bool pdl);
+// Zeros of L right of each row's 64-wide diagonal block (columns >= 64 * (r / 64 + 1)).
+int launch_zero_upper(float* L, int64_t batch, int64_t n, cudaStream_t q, bool pdl);
 // Tinv (+ m * tstride, leading dimension tld) receives inv(L_kk) as a 64 x 64 lower triangle.
 int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, int64_t stride,
                        int64_t ld, int64_t batch, int64_t k, int64_t kb, float* Tinv, int* info,

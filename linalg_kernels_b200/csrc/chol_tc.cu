@@ -318,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row_base = c.tm * kBM + q * 32;  // first row of this warp's quarter
       const int64_t col0 = c.tn * BN;
       float* cbase = g.C + c.mi * g.cstride;
+      const float* sbase = (g.Csrc != nullptr ? g.Csrc : g.C) + c.mi * g.cstride;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         const int64_t gc0 = col0 + cc * 32;
@@ -345,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int rr = 0; rr < 8; ++rr) {
           const int64_t grow = row_base + rr * 4 + sub_r;
           float* cp = cbase + grow * g.ldc + col;
+          const float* sp = sbase + grow * g.ldc + col;
           lim[rr] = grow >= g.m ? -1
                                 : (g.lower_only ? (grow + g.diag_offset - shift < g.ncols - 1
                                                        ? grow + g.diag_offset - shift
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                 : g.ncols - 1);
           vec[rr] = col + 3 <= lim[rr] && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0);
           cv[rr] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (vec[rr] && g.beta != 0.f) cv[rr] = *reinterpret_cast<const float4*>(cp);
+          if (vec[rr] && g.beta != 0.f) cv[rr] = *reinterpret_cast<const float4*>(sp);
         }
 #pragma unroll
         for (int rr = 0; rr < 8; ++rr) {
@@ -361,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t grow = row_base + tr;
           const float4 a4 = *reinterpret_cast<const float4*>(tile + tr * Cfg::EPI_LD + sub_c);
           float* cp = cbase + grow * g.ldc + col;
+          const float* sp = sbase + grow * g.ldc + col;
           if (vec[rr]) {
             float4 o;
             o.x = fmaf(g.alpha, a4.x, g.beta * cv[rr].x);
@@ -373,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               if (col + e > lim[rr]) break;
-              cp[e] = (g.beta != 0.f) ? fmaf(g.alpha, av[e], g.beta * cp[e]) : g.alpha * av[e];
+              cp[e] = (g.beta != 0.f) ? fmaf(g.alpha, av[e], g.beta * sp[e]) : g.alpha * av[e];
             }
           }
         }

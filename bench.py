@@ -84,6 +84,11 @@ class Dist:
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.local))
             self.pg = dist
+            # the first collectives set up NCCL's connections, partly in the background:
+            # done here, before any timed region
+            for _ in range(2):
+                dist.barrier(device_ids=[self.local])
+            torch.cuda.synchronize()
 
     def barrier(self):
         if self.pg:

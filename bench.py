@@ -611,7 +611,9 @@ def _other_shapes(args, skip, dev, peaks, peak_kind, lib):
     for name in names:
         cfg = inputs.CONFIGS[name]
         pool, pool_bytes = _pool(cfg, dev, 0, max_inputs=16)
-        steps = max(3, min(args.steps, 20))
+        # enough calls that the timed region is ~ms long (the event bracket's fixed cost
+        # is then noise): 200 for the microsecond shapes, at most 20 for the others
+        steps = 200 if cfg.n <= 64 else max(3, min(args.steps, 20))
         total, per = _time_steps(custom_kernel, pool, steps, 3, _NoDist())
         ms = total / steps
         value = cfg.batch / (ms / 1e3)
@@ -711,7 +713,7 @@ def run_ncu_target(args):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default=DEFAULT_CONFIG)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")

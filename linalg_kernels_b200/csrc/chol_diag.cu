@@ -21,10 +21,10 @@
 // that records CHOL_ERR_WAIT_TIMEOUT in the status word and lets every waiter return) and
 // read tiles through L2 (ld.global.cg).
 //
-// Factors: the register-resident warp factor (warp_potrf_rows) and the column-parallel
-// inverse are fully unrolled, several thousand instructions that a task runs once. The
-// diagonal tasks after D(0) run both once on scratch data while they wait for their inputs,
-// so the real run starts with this SM's instruction cache warm.
+// Factors: the register-resident warp factor (warp_potrf_rows) and the blocked inverse
+// (inverse_blocked64) are fully unrolled, several thousand instructions that a task runs
+// once. The diagonal tasks after D(0) run both once on scratch data while they wait for
+// their inputs, so the real run starts with this SM's instruction cache warm.
 //
 // This replaces the per-step chain of the blocked schedule for the block — 3 launches per
 // 64 columns (left-looking GEMM, potrf_block, solve GEMM), each bound by launch and pipeline
@@ -222,19 +222,81 @@ __device__ __forceinline__ void to_array(float (&m)[4][4], const float2 (&acc)[4
   }
 }
 
-// The unrolled warp factor and the column-parallel inverse, each as ONE function: every call
-// site (and the warm-up run) executes the same instructions, and their register needs stay
-// apart from the task code around them.
+// The unrolled warp factor and the blocked inverse, each as ONE function: every call site
+// (and the warm-up run) executes the same instructions, and their register needs stay apart
+// from the task code around them.
 __device__ __noinline__ int warp_factor64(float* S, float* col, float* rdiag, int lane) {
   return tile64_potrf<kDLD>(S, col, rdiag, lane);
 }
-// Column c of T = inv(L) into Ts (row-major, stride kDLD), one thread per column.
-__device__ __noinline__ void inverse_column64(const float* S, const float* rdiag, float* Ts,
-                                              int c) {
-  float t[64];
-  tile64_inverse_column<kDLD>(S, rdiag, c, t);
+// T = inv(L) for the factored 64 x 64 block in S as a 2 x 2 block inverse, all kDT threads:
+//   T11 = inv(L11), T22 = inv(L22)      (32-row forward substitutions, side by side:
+//                                        thread c < 64 computes column c of its block)
+//   T21 = -T22 (L21 T11)                (two 32 x 32 x 32 products, 4 outputs per thread)
+// Half the dependent chain of the column-by-column inverse. W: 32 x kDLD floats of scratch.
+__device__ __noinline__ void inverse_blocked64(const float* S, const float* rdiag, float* Ts,
+                                               float* W) {
+  const int t = threadIdx.x;
+  if (t < 64) {
+    const int c = t, base = (t < 32) ? 0 : 32;  // column c of the diagonal block at base
+    float x[32];
 #pragma unroll
-  for (int r = 0; r < 64; ++r) Ts[r * kDLD + c] = t[r];
+    for (int i = 0; i < 32; ++i) {
+      const float* rp = S + (base + i) * kDLD + base;
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < i / 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(rp + 4 * q);
+        acc = ffma2(make_float2(v.x, v.y), make_float2(x[4 * q], x[4 * q + 1]), acc);
+        acc = ffma2(make_float2(v.z, v.w), make_float2(x[4 * q + 2], x[4 * q + 3]), acc);
+      }
+      float sum = acc.x + acc.y;
+#pragma unroll
+      for (int m = (i / 4) * 4; m < i; ++m) sum = fmaf(rp[m], x[m], sum);
+      const float ri = rdiag[base + i];
+      const int cc = c - base;
+      x[i] = (i == cc) ? ri : ((i < cc) ? 0.f : -ri * sum);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) Ts[(base + i) * kDLD + c] = x[i];
+    if (base == 32) {  // the block above T22 is zero (T21, below T11, follows)
+#pragma unroll
+      for (int i = 0; i < 32; ++i) Ts[i * kDLD + c] = 0.f;
+    }
+  }
+  __syncthreads();
+  const int i = t >> 3, j0 = (t & 7) * 4;  // output row i, columns j0..j0+3 of a 32 x 32 block
+  {
+    // W = L21 T11 (T11 lower: k >= j)
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* lrow = S + (32 + i) * kDLD;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float a = lrow[k];
+      const float4 b = *reinterpret_cast<const float4*>(Ts + k * kDLD + j0);
+      o.x = fmaf(a, b.x, o.x);
+      o.y = fmaf(a, b.y, o.y);
+      o.z = fmaf(a, b.z, o.z);
+      o.w = fmaf(a, b.w, o.w);
+    }
+    *reinterpret_cast<float4*>(W + i * kDLD + j0) = o;
+  }
+  __syncthreads();
+  {
+    // T21 = -T22 W (T22 lower: k <= i)
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* trow = Ts + (32 + i) * kDLD + 32;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float a = trow[k];
+      const float4 b = *reinterpret_cast<const float4*>(W + k * kDLD + j0);
+      o.x = fmaf(a, b.x, o.x);
+      o.y = fmaf(a, b.y, o.y);
+      o.z = fmaf(a, b.z, o.z);
+      o.w = fmaf(a, b.w, o.w);
+    }
+    *reinterpret_cast<float4*>(Ts + (32 + i) * kDLD + j0) = make_float4(-o.x, -o.y, -o.z, -o.w);
+  }
+  __syncthreads();
 }
 
 // Publish: every thread's global stores, then the flag (release at GPU scope).
@@ -249,6 +311,7 @@ __device__ __forceinline__ void publish(int* flag, int epoch) {
 __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   __shared__ __align__(16) float Xs[64 * kDLD];
   __shared__ __align__(16) float Ys[64 * kDLD];
+  __shared__ __align__(16) float Ws[32 * kDLD];  // scratch of the blocked inverse
   __shared__ __align__(16) float col[128];
   __shared__ float rdiag[64];
   __shared__ unsigned s_ticket;
@@ -302,8 +365,7 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
       __syncthreads();
       if (tid < 32) warp_factor64(Ys, col, rdiag, tid);
       __syncthreads();
-      if (tid < 64) inverse_column64(Ys, rdiag, Xs, tid);
-      __syncthreads();
+      inverse_blocked64(Ys, rdiag, Xs, Ws);
     }
     for (int p = 0; p < j; ++p) {
       if (!cta_wait(&F[kFlagO + i * 16 + p], ep, a.status)) return;
@@ -381,8 +443,7 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   }
   __syncthreads();
   const int f = s_flag[0];
-  if (tid < 64) inverse_column64(Ys, rdiag, Xs, tid);
-  __syncthreads();
+  inverse_blocked64(Ys, rdiag, Xs, Ws);
   float* dl = tileL(d, d);
   float* dv = tileT(d);
   for (int e = tid; e < 64 * 16; e += kDT) {

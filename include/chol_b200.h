@@ -204,7 +204,9 @@ CHOL_API int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t 
    with cudaMalloc on first need); otherwise left-looking 64-wide steps (diagonal block +
    inverse, solve of the rows below). Tinv: 64*64 floats of device workspace (used by the
    64-wide steps). info (nullable, one int): first failing column of the panel (1-based) or
-   0. The per-panel step of the multi-GPU block-column-cyclic driver. */
+   0. The per-panel step of the multi-GPU block-column-cyclic driver. The cached scratch is
+   shared by every call on the device: calls that overlap on the GPU (different queues)
+   race on it. */
 CHOL_API int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv,
                                   int* info, void* queue);
 
@@ -212,7 +214,10 @@ CHOL_API int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, fl
    of C (and row c of Q) stands for global column c + (c / col_block) * (col_stride -
    col_block), and lower_only compares that global column with the row. One launch updates
    every trailing block a rank owns. col_block must be 256 and col_stride a multiple of it
-   (tensor-core path; needs 16-byte aligned rows). */
+   (tensor-core path; needs 16-byte aligned rows). With P == Q (the driver's case) the TF32
+   low parts of P are computed once into a scratch buffer the library caches per device
+   (grown with cudaMalloc on first need; calls that overlap on the GPU race on it) and
+   loaded by the GEMM instead of split in shared memory. */
 CHOL_API int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t ncols, int64_t K,
                                      const float* P, int64_t ldp, const float* Q, int64_t ldq,
                                      float alpha, float beta, int64_t diag_offset, int lower_only,

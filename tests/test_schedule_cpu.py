@@ -1,0 +1,68 @@
+"""CPU: the host side of the schedule choice, through the C ABI without a GPU.
+
+chol_launch_count and chol_workspace_bytes are pure host logic; they follow the schedules
+the blocked path picks: one small-kernel launch for n <= 64; for one panel, the whole matrix
+in one diagonal-block launch while batch * n^3 is small, else the 64-wide chain (a zero fill,
+then per 64 columns a factor, a left-looking update and a solve); for several 512-wide
+panels, per panel the diagonal block, the solve GEMM, the split and the trailing update.
+Also the reference arm of bench.py (the reference's CPU path) prints its JSON line."""
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+from linalg_kernels_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.mark.parametrize("batch,n,launches", [
+    (1, 32, 1), (4096, 32, 1), (1024, 64, 1),
+    (4, 256, 2),            # one diagonal-block launch (+ copy)
+    (640, 512, 23),         # chain: zero fill + 8 factors + 7 updates + 7 solves
+    (60, 1024, 47),         # chain: 1 + 16 + 15 + 15
+    (3, 200, 11),           # chain with a ragged last block: 1 + 4 + 3 + 3
+    (1, 2048, 14),          # 3 x (block, solve, split, trailing) + last block + copy
+    (1, 2100, 18),          # 4 full panels + a 52-wide last panel (one factor) + copy
+    (1, 16384, 126),        # 31 x 4 + last block + copy
+    (2, 1030, 50),          # rows not 16-byte multiples: the 64-wide steps in each panel
+])
+def test_launch_counts_follow_the_schedule(batch, n, launches):
+    assert int(_lib.load().chol_launch_count(batch, n)) == launches
+
+
+def test_workspace_regions():
+    lib = _lib.load()
+    ws = lambda b, n: int(lib.chol_workspace_bytes(b, n))
+    assert ws(1024, 64) == 0                           # small kernel: no workspace
+    # required region: one 64 x 64 inverse block and one counter per matrix
+    required = lambda b: b * 64 * 64 * 4 + ((b * 4 + 255) // 256) * 256
+    # one panel, large batch (chain): only the required region
+    assert ws(640, 512) == required(640)
+    # one panel, small batch (diagonal-block kernel): + n/64 inverse blocks and the tile
+    # flags per matrix, + a ticket counter
+    assert ws(4, 256) == required(4) + 4 * (4 * 64 * 64 * 4 + 768 * 4) + 256
+    # several panels: + panel buffer (n x 512), V (512 x 512), flags, one ticket per panel
+    n = 2048
+    assert ws(1, n) == required(1) + n * 512 * 4 + 512 * 512 * 4 + 768 * 4 + 256
+    # rows that are not 16-byte multiples: only the required region
+    assert ws(2, 1030) == required(2)
+
+
+def test_reference_arm_prints_its_line():
+    out = subprocess.run(
+        [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "3",
+         "--warmup", "3", "--cpu-budget", "0.5"],
+        capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["metric"] == "matrices/s" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "reference"
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0

@@ -132,6 +132,19 @@ def check(status: int, where: str) -> None:
         raise CholeskyError(status, where)
 
 
+def fast_call():
+    """(binding, queue getter) for the hot path: the chol_potrf_batched_ws_f32 binding (as
+    potrf_ws takes it) and a function mapping a device index to the raw handle of torch's
+    current queue there; None when torch has no raw getter."""
+    import torch
+
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is None:
+        return None
+    potrf_ws(0, 0, 0, 0, 0, 0, 0, 0)  # resolves the binding (an empty call does nothing)
+    return _pyext, raw
+
+
 def current_queue(device) -> int:
     """Raw handle of torch's current CUDA queue on ``device`` (0 = legacy default)."""
     import torch

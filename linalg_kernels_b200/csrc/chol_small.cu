@@ -43,22 +43,45 @@ constexpr int small_lpm() {
 template <int NP>
 using SmallShape = WarpShape<NP, small_lpm<NP>()>;
 
-// Staging tile of one matrix: NP rows of stride NP+4 floats for the loads, reused as
-// NP/32 128B-swizzled 32-column tiles for the tensor store; rounded to 1 KiB (the swizzled
-// layout needs 1024-byte aligned tiles).
-template <int NP>
+// Staging of one matrix.
+// Tensor-store layout (n = 32 and n = 64 with aligned rows): the factor is written back as
+// 32 x 32 tiles in the 128-byte-swizzled layout of the tensor store (16-byte chunk k of
+// tile row r at slot k ^ (r & 7)) and leaves with one tensor store per tile. At n = 64 the
+// loads use the same layout (conflict-free row reads without padding) and only three tiles
+// are kept: the one above the diagonal is never read and is stored from a zero tile shared
+// by the CTA, 12 KiB per matrix against 17 KiB of padded rows, so 4 CTAs fit per SM and
+// back-to-back calls overlap further (b=1024: 9.9 -> 9.1 us per call). At n = 32 the loads
+// keep padded rows (measured faster there: more CTAs per SM did not pay).
+// Otherwise: NP rows of stride NP + 4 floats, rounded to 1 KiB.
+template <int NP, bool FULL>
+constexpr bool small_quad() {  // tensor-store layout for the write-back and the stores
+  return FULL && NP >= 32;
+}
+template <int NP, bool FULL>
+constexpr bool small_quad_load() {  // ... and for the loads
+  return FULL && NP == 64;
+}
+template <int NP, bool FULL>
 constexpr int small_tile_floats() {
-  return ((NP * (NP + 4) * 4 + 1023) / 1024) * 1024 / 4;
+  return small_quad_load<NP, FULL>() ? 3 * 1024
+                                     : ((NP * (NP + 4) * 4 + 1023) / 1024) * 1024 / 4;
 }
-template <int NP>
+template <int NP, bool FULL>
+constexpr int small_zero_floats() {
+  return small_quad_load<NP, FULL>() ? 1024 : 0;
+}
+template <int NP, bool FULL>
 constexpr size_t small_smem_bytes() {
-  return size_t(small_warps<NP>()) * SmallShape<NP>::MPW *
-             (size_t(small_tile_floats<NP>()) + SmallShape<NP>::COLS) * 4 + 1024;
+  return (size_t(small_zero_floats<NP, FULL>()) +
+          size_t(small_warps<NP>()) * SmallShape<NP>::MPW *
+              (size_t(small_tile_floats<NP, FULL>()) + SmallShape<NP>::COLS)) * 4 + 1024;
 }
-// The tensor-store path covers n = 32 and n = 64 (rows of 128-byte multiples).
+// Float offset of element (r, c) in the quadrant layout (c % 4 == 0 for a 16-byte chunk).
 template <int NP>
-constexpr bool small_tma_store() {
-  return NP >= 32;
+__device__ __forceinline__ int quad_off(int r, int c) {
+  const int t = (NP == 64 && r >= 32) ? ((c >= 32) ? 2 : 1) : 0;
+  const int rr = r & 31, cc = c & 31;
+  return t * 1024 + rr * 32 + ((((cc >> 2) ^ (rr & 7))) << 2) + (cc & 3);
 }
 
 // FULL: n == NP and 16-byte aligned rows (vector path). Otherwise scalar loads with
@@ -81,14 +104,23 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
   constexpr int R = SmallShape<NP>::R;
   constexpr int MPW = SmallShape<NP>::MPW;
   constexpr int LDS = NP + 4;
-  constexpr int TILE = small_tile_floats<NP>();
-  constexpr bool TMA_OUT = FULL && small_tma_store<NP>();
+  constexpr int TILE = small_tile_floats<NP, FULL>();
+  constexpr bool QUAD = small_quad<NP, FULL>();       // write-back layout, tensor stores
+  constexpr bool QLOAD = small_quad_load<NP, FULL>();  // load layout
+  constexpr int ZF = small_zero_floats<NP, FULL>();
   extern __shared__ __align__(1024) float4 smem_raw[];
-  float* smem = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                         ~uintptr_t(1023));
+  float* zero_tile = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  float* smem = zero_tile + ZF;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (ZF > 0) {
+    // the tile above the diagonal of every n = 64 output, stored by TMA from here
+    for (int i = threadIdx.x; i < ZF; i += blockDim.x) zero_tile[i] = 0.f;
+    fence_proxy_async_smem();
+    __syncthreads();
+  }
   const int grp = lane / LPM;
   const int gl = lane % LPM;
   float* stage = smem + size_t(warp) * MPW * TILE;
@@ -114,7 +146,9 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
 #pragma unroll
         for (int idx = lane; idx < NP * C4; idx += 32) {
           const int r = idx / C4, c4 = idx % C4;
-          if (c4 * 4 <= r) cp_async16(st + r * LDS + c4 * 4, src + r * NP + c4 * 4);
+          if (c4 * 4 <= r)
+            cp_async16(QLOAD ? st + quad_off<NP>(r, c4 * 4) : st + r * LDS + c4 * 4,
+                       src + r * NP + c4 * 4);
         }
         rpad = NP;
       } else {
@@ -129,7 +163,12 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
     // identity padding: rows rpad..NP-1 (all rows when the matrix is past the batch)
     for (int idx = lane; idx < (NP - rpad) * NP; idx += 32) {
       const int r = rpad + idx / NP, c = idx % NP;
-      st[r * LDS + c] = (r == c) ? 1.f : 0.f;
+      if (QLOAD) {
+        if (NP == 64 && r < 32 && c >= 32) continue;  // no storage above the diagonal tile
+        st[quad_off<NP>(r, c)] = (r == c) ? 1.f : 0.f;
+      } else {
+        st[r * LDS + c] = (r == c) ? 1.f : 0.f;
+      }
     }
   }
   cp_async_wait_all();
@@ -140,10 +179,12 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
   const float* mst = stage + grp * TILE;
 #pragma unroll
   for (int s = 0; s < R; ++s) {
-    const float* rp = mst + (s * LPM + gl) * LDS;
+    const int row = s * LPM + gl;
+    const float* rp = mst + row * LDS;
 #pragma unroll
     for (int q = 0; q < (s + 1) * LPM / 4; ++q) {
-      const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(rp + 4 * q);
+      const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(
+          QLOAD ? mst + quad_off<NP>(row, 4 * q) : rp + 4 * q);
       a[s][2 * q] = v.x;
       a[s][2 * q + 1] = v.y;
     }
@@ -176,11 +217,10 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
           bad[s] = !(dg > 0.f);
         }
       }
-      if (TMA_OUT) {
-        // 128B-swizzled 32-column tiles: chunk qh of row i at slot qh ^ (i & 7)
-        const int h = q >> 3, qh = q & 7;
-        float* tile = stage + grp * TILE + h * (NP * 32);
-        *reinterpret_cast<float4*>(tile + i * 32 + ((qh ^ (i & 7)) << 2)) = v;
+      if (QUAD) {
+        // quadrant layout (no storage for the tile above the diagonal at n = 64)
+        if (!(NP == 64 && i < 32 && q >= 8))
+          *reinterpret_cast<float4*>(stage + grp * TILE + quad_off<NP>(i, 4 * q)) = v;
       } else {
         *reinterpret_cast<float4*>(rp + 4 * q) = v;
       }
@@ -199,20 +239,28 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
 
   // ---- store. n = 32/64: one tensor store per 32-column half of each matrix from the
   // swizzled tiles; smaller full sizes: one bulk copy per row; otherwise 4-byte stores ----
-  if (TMA_OUT) {
+  if (QUAD) {
     fence_proxy_async_smem();
     __syncwarp();
     if (lane < MPW) {
       const int64_t m = mbase + lane;
       if (m < batch) {
+        // one 32 x 32 tensor store per tile (box 32 x 32); at n = 64 the tile above the
+        // diagonal comes from the zero tile
         const float* base = stage + lane * TILE;
-#pragma unroll
-        for (int h = 0; h < NP / 32; ++h)
+        auto store_tile = [&](int x, int y, const float* src) {
           asm volatile(
               "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::
                   "l"(reinterpret_cast<uint64_t>(&out_map)),
-              "r"(h * 32), "r"(0), "r"(int(m)), "r"(smem_u32(base + h * (NP * 32)))
+              "r"(x), "r"(y), "r"(int(m)), "r"(smem_u32(src))
               : "memory");
+        };
+        store_tile(0, 0, base);
+        if (NP == 64) {
+          store_tile(0, 32, base + 1024);
+          store_tile(32, 32, base + 2048);
+          store_tile(32, 0, zero_tile);
+        }
       }
       bulk_store_wait_read();
     }
@@ -366,12 +414,13 @@ int launch_np(const float* A, float* L, int64_t batch, int n, int* info, cudaStr
   constexpr int MPC = small_warps<NP>() * SmallShape<NP>::MPW;
   const int64_t blocks = (batch + MPC - 1) / MPC;
   if (blocks > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
-  const size_t smem = small_smem_bytes<NP>();
   const bool full = (n == NP) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0) &&
                     ((reinterpret_cast<uintptr_t>(L) & 15) == 0);
+  const size_t smem = full ? small_smem_bytes<NP, true>() : small_smem_bytes<NP, false>();
   alignas(64) CUtensorMap map;
   memset(&map, 0, sizeof(map));
-  if (full && small_tma_store<NP>() && !cached_out_map(&map, L, batch, n, NP))
+  // tensor stores of 32 x 32 tiles (the quadrant layout)
+  if (full && small_quad<NP, true>() && !cached_out_map(&map, L, batch, n, 32))
     return CHOL_ERR_UNSUPPORTED;
   cudaError_t e;
   SmallCall call;
@@ -418,11 +467,11 @@ template <int NP>
 cudaError_t set_smem_np() {
   cudaError_t e = cudaFuncSetAttribute(small_potrf_kernel<NP, true>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(small_smem_bytes<NP>()));
+                                       int(small_smem_bytes<NP, true>()));
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(small_potrf_kernel<NP, false>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(small_smem_bytes<NP>()));
+                              int(small_smem_bytes<NP, false>()));
 }
 
 }  // namespace

@@ -43,11 +43,14 @@ import torch  # noqa: E402
 DEFAULT_CONFIG = "b1024n64"
 L2_BYTES = 126 * 1024 * 1024
 
-# The reference's published single-B200 times for these shapes (references/CURRENT_PERF.md),
-# converted to matrices/s: batch / time.
+# The reference's published single-B200 times per call for the benchmark grid: the seven
+# configs as the reference's best snapshots (references/CURRENT_PERF.md, NEW_PERF3.md for
+# b64n256, b640n512, b60n1024), the other eight from references/CURRENT_PERF.md.
 REFERENCE_PUBLISHED_S = {
     "b4096n32": 15.7e-6, "b1024n64": 24.1e-6, "b64n256": 191e-6, "b640n512": 2.88e-3,
     "b60n1024": 2.20e-3, "b1n16384": 15.1e-3, "b1n32768": 42.9e-3,
+    "b256n128": 70.9e-6, "b16n512": 537e-6, "b4n1024": 1199e-6, "b2n2048": 3.21e-3,
+    "b8n2048": 4.88e-3, "b1n4096": 1527e-6, "b2n4096": 11.1e-3, "b1n8192": 6.37e-3,
 }
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of the
@@ -271,7 +274,7 @@ def run_reference(args, dist: Dist):
     """Reference arm: the reference's own CPU implementation of the path on the host cores."""
     from linalg_kernels_b200 import inputs
 
-    cfg = inputs.CONFIGS[args.config]
+    cfg = inputs.GRID[args.config]
     if dist.rank != 0:
         return
     if torch.cuda.is_available():
@@ -318,7 +321,7 @@ def run_ours(args, dist: Dist):
     dev = torch.device("cuda", dist.local if dist.world > 1 else 0)
     torch.cuda.set_device(dev)
     peaks, peak_kind = _peaks()
-    cfg = inputs.CONFIGS[args.config]
+    cfg = inputs.GRID[args.config]
     n, b = cfg.n, cfg.batch
     pool, pool_bytes = _pool(cfg, dev, dist.rank, max_inputs=32)
     launches_per_call = int(lib.chol_launch_count(b, n))
@@ -369,6 +372,7 @@ def run_ours(args, dist: Dist):
     }
     if shapes is not None:
         line["shapes"] = shapes
+        line["grid"] = _grid_summary(cfg.name, ms_step, shapes)
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -554,7 +558,7 @@ def run_cyclic(args, dist: Dist):
     dev = torch.device("cuda", dist.local)
     torch.cuda.set_device(dev)
     peaks, peak_kind = _peaks()
-    cfg = inputs.CONFIGS[args.config]
+    cfg = inputs.GRID[args.config]
     n = cfg.n
     lay = CyclicLayout(n, dist.world, dist.rank, 256)
     g = torch.Generator(device=dev).manual_seed(cfg.seed)
@@ -629,13 +633,13 @@ def _other_shapes(args, skip, dev, peaks, peak_kind, lib):
     from linalg_kernels_b200.cholesky import custom_kernel
 
     out = []
-    names = [k for k in inputs.CONFIGS if k != skip and (args.big or k != "b1n32768")]
+    names = [k for k in inputs.GRID if k != skip and (args.big or k != "b1n32768")]
     for name in names:
-        cfg = inputs.CONFIGS[name]
+        cfg = inputs.GRID[name]
         pool, pool_bytes = _pool(cfg, dev, 0, max_inputs=16)
         # enough calls that the timed region is ~ms long (the event bracket's fixed cost
         # is then noise): 200 for the microsecond shapes, at most 20 for the others
-        steps = 200 if cfg.n <= 64 else max(3, min(args.steps, 20))
+        steps = 200 if cfg.n <= 128 else max(3, min(args.steps, 20))
         total, per = _time_steps(custom_kernel, pool, steps, 3, _NoDist())
         ms = total / steps
         value = cfg.batch / (ms / 1e3)
@@ -652,6 +656,19 @@ def _other_shapes(args, skip, dev, peaks, peak_kind, lib):
         del pool
         torch.cuda.empty_cache()
     return out
+
+
+def _grid_summary(name, ms_step, shapes):
+    """The reference leaderboard's ranking figure (AGENTS.md:58-64): the geometric mean of the
+    per-call runtimes over the benchmark-grid entries, ours and the reference's published,
+    over the same entries (b1n32768 only with --big)."""
+    ms = {row["workload"]: row["ms_per_step"] for row in shapes}
+    ms[name] = ms_step
+    names = [k for k in ms if k in REFERENCE_PUBLISHED_S]
+    ours = math.exp(sum(math.log(ms[k]) for k in names) / len(names))
+    ref = math.exp(sum(math.log(REFERENCE_PUBLISHED_S[k] * 1e3) for k in names) / len(names))
+    return {"entries": len(names), "geomean_ms": ours, "reference_geomean_ms": ref,
+            "vs_reference_published": ref / ours}
 
 
 GEMM_PROBES = {
@@ -720,7 +737,7 @@ def run_ncu_target(args):
     from linalg_kernels_b200 import inputs
     from linalg_kernels_b200.cholesky import custom_kernel
 
-    cfg = inputs.CONFIGS[args.config]
+    cfg = inputs.GRID[args.config]
     dev = torch.device("cuda", 0)
     gen_dev = "cpu" if cfg.n <= 1024 else dev
     a, _ = inputs.config_input(cfg, device=gen_dev)

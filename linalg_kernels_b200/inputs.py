@@ -33,7 +33,7 @@ class Config:
     seed: int
 
 
-# The benchmark configs; seeds follow the reference's benchmark seeds (AGENTS.md:74-88).
+# The benchmark configs; seeds follow the reference's benchmark seeds (AGENTS.md:67-81).
 CONFIGS: dict[str, Config] = {c.name: c for c in [
     Config("b4096n32", 4096, 32, "spectral", 1e2, 41032),
     Config("b1024n64", 1024, 64, "spectral", 1e3, 41064),
@@ -43,6 +43,52 @@ CONFIGS: dict[str, Config] = {c.name: c for c in [
     Config("b1n16384", 1, 16384, "covariance", 0.5, 48284),
     Config("b1n32768", 1, 32768, "covariance", 0.5, 48368),
 ]}
+
+# The reference's whole benchmark grid (AGENTS.md:66-81; its leaderboard ranks by the
+# geometric mean of the runtimes over these 15 entries): the configs above plus the other
+# eight shapes, with the reference's seeds. The reference's generator is not available; the
+# family follows the nearest config (spectral up to n = 256, covariance above, shift 0.5
+# from n = 2048 on, as at n = 16384).
+GRID: dict[str, Config] = {c.name: c for c in [
+    CONFIGS["b4096n32"],
+    CONFIGS["b1024n64"],
+    Config("b256n128", 256, 128, "spectral", 1e3, 41128),
+    CONFIGS["b64n256"],
+    Config("b16n512", 16, 512, "covariance", 1.0, 41512),
+    CONFIGS["b640n512"],
+    Config("b4n1024", 4, 1024, "covariance", 1.0, 42024),
+    CONFIGS["b60n1024"],
+    Config("b2n2048", 2, 2048, "covariance", 0.5, 44048),
+    Config("b8n2048", 8, 2048, "covariance", 0.5, 512048),
+    Config("b1n4096", 1, 4096, "covariance", 0.5, 48096),
+    Config("b2n4096", 2, 4096, "covariance", 0.5, 514096),
+    Config("b1n8192", 1, 8192, "covariance", 0.5, 48192),
+    CONFIGS["b1n16384"],
+    CONFIGS["b1n32768"],
+]}
+
+
+@dataclass(frozen=True)
+class ShapeSpec:
+    batch: int
+    n: int
+    seed: int
+    case: str | None = None  # None: the family of the benchmark grid at this n
+
+
+# The reference's 17 test shapes (AGENTS.md:83-100) with their seeds and structural cases.
+# Their "cond" field is a dynamic-range control of the reference's own generator; our case
+# generators use fixed constants instead.
+TEST_SHAPES: tuple[ShapeSpec, ...] = (
+    ShapeSpec(16, 32, 53124), ShapeSpec(16, 64, 53125), ShapeSpec(16, 128, 3321),
+    ShapeSpec(8, 256, 94010), ShapeSpec(4, 512, 32523), ShapeSpec(2, 1024, 4327),
+    ShapeSpec(1, 2048, 224466),
+    ShapeSpec(8, 128, 1200, "spectrum"), ShapeSpec(8, 128, 1201, "diagonal"),
+    ShapeSpec(32, 32, 1202, "spectrum"), ShapeSpec(32, 32, 1203, "diagonal"),
+    ShapeSpec(16, 64, 1204, "spectrum"), ShapeSpec(16, 64, 1205, "diagonal"),
+    ShapeSpec(4, 256, 32524, "lowrank"), ShapeSpec(4, 512, 32525, "rowscale"),
+    ShapeSpec(4, 512, 32526, "tridiagonal"), ShapeSpec(2, 1024, 4330, "lowrank"),
+)
 
 
 class _NoTF32:
@@ -94,13 +140,22 @@ def covariance(batch: int, n: int, shift: float, seed: int, device="cpu"):
 
 
 def config_input(cfg: Config | str, device="cpu", batch: int | None = None):
-    """(A, cond) for a named benchmark config (optionally with a smaller batch)."""
+    """(A, cond) for a named benchmark-grid entry (optionally with a smaller batch)."""
     if isinstance(cfg, str):
-        cfg = CONFIGS[cfg]
+        cfg = GRID[cfg]
     b = cfg.batch if batch is None else batch
     if cfg.family == "spectral":
         return spectral(b, cfg.n, cfg.param, cfg.seed, device)
     return covariance(b, cfg.n, cfg.param, cfg.seed, device)
+
+
+def spec_input(shape: ShapeSpec, device="cpu") -> torch.Tensor:
+    """The input of one of the reference's test shapes (float32, contiguous)."""
+    if shape.case is not None:
+        return case(shape.case, shape.batch, shape.n, shape.seed, device)
+    if shape.n <= 256:
+        return spectral(shape.batch, shape.n, 1e3, shape.seed, device)[0]
+    return covariance(shape.batch, shape.n, 1.0, shape.seed, device)[0]
 
 
 def case(name: str, batch: int, n: int, seed: int, device="cpu") -> torch.Tensor:

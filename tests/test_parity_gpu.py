@@ -96,7 +96,7 @@ def test_diagonal_known_answer():
 
 
 def _check_full_config(name, batch=None):
-    cfg = inputs.CONFIGS[name]
+    cfg = inputs.GRID[name]
     a, cond = inputs.config_input(cfg, device=DEV, batch=batch)
     return _check_input(a, cond)
 
@@ -132,6 +132,22 @@ def test_baseline_configs_full_size(name):
 
 def test_baseline_config_n16384():
     _check_full_config("b1n16384")
+
+
+# the rest of the reference's benchmark grid (AGENTS.md:66-81), full size
+@pytest.mark.parametrize("name", [k for k in inputs.GRID if k not in inputs.CONFIGS])
+def test_benchmark_grid_full_size(name):
+    _check_full_config(name)
+
+
+# the reference's 17 test shapes (AGENTS.md:83-100) with their seeds and structural cases;
+# cond(A) from the FP64 eigenvalues
+@pytest.mark.parametrize("spec", inputs.TEST_SHAPES,
+                         ids=lambda s: f"b{s.batch}n{s.n}-{s.case or 'family'}-{s.seed}")
+def test_reference_test_shapes(spec):
+    a = inputs.spec_input(spec, device=DEV)
+    ev = torch.linalg.eigvalsh(a.double())
+    _check_input(a, ev[:, -1] / ev[:, 0])
 
 
 def test_non_contiguous_input():

@@ -345,6 +345,10 @@ def run_ours(args, dist: Dist):
     if dist.world == 1 and not args.no_cpu_baseline:
         cpu = _cpu_reference_rate(cfg, pool[0].cpu(), budget_s=args.cpu_budget)
 
+    validator = None
+    if dist.world == 1 and args.validate:
+        validator = _validator_timing(dev, peaks, peak_kind, lib)
+
     shapes = None
     if dist.world == 1 and args.shapes:
         shapes = _other_shapes(args, cfg.name, dev, peaks, peak_kind, lib)
@@ -373,6 +377,8 @@ def run_ours(args, dist: Dist):
     if shapes is not None:
         line["shapes"] = shapes
         line["grid"] = _grid_summary(cfg.name, ms_step, shapes)
+    if validator is not None:
+        line["validator"] = validator
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -658,6 +664,54 @@ def _other_shapes(args, skip, dev, peaks, peak_kind, lib):
     return out
 
 
+def _validator_timing(dev, peaks, peak_kind, lib, names=("b1024n64", "b640n512", "b1n16384")):
+    """The device-side checker (chol_validate_f32: the residual tiles in FP64, then the scan
+    of L) on factors of grid inputs: time per call and its rates. Work per matrix: the lower
+    triangle of tril(L) tril(L)^T, sum_c (c + 1)(n - c) ~ n^3/6 FP64 multiply-adds (n^3/3
+    flops); bytes: A's lower triangle and L read once each (4 n^2 + ...) at least."""
+    from linalg_kernels_b200 import _lib, inputs
+    from linalg_kernels_b200.cholesky import custom_kernel
+
+    rows = []
+    for name in names:
+        cfg = inputs.GRID[name]
+        a, _ = inputs.config_input(cfg, device=dev)
+        l = custom_kernel(a)
+        b, n = cfg.batch, cfg.n
+        out = torch.empty(b, 8, dtype=torch.float64, device=dev)
+        work = torch.empty(int(lib.chol_validate_work_bytes(b, n)), dtype=torch.uint8, device=dev)
+        q = ctypes.c_void_p(_lib.current_queue(dev))
+
+        def call():
+            _lib.check(lib.chol_validate_f32(ctypes.c_void_p(a.data_ptr()),
+                                             ctypes.c_void_p(l.data_ptr()), b, n,
+                                             ctypes.c_void_p(out.data_ptr()),
+                                             ctypes.c_void_p(work.data_ptr()), q),
+                       "chol_validate_f32")
+
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        reps = 5
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            call()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / reps / 1e3
+        flops = 2.0 * b * sum((c + 1) * (n - c) for c in range(n))
+        bytes_ = 8.0 * b * n * n
+        st = out.cpu()
+        rows.append({"workload": name, "ms": t * 1e3, "fp64_tflops": flops / t / 1e12,
+                     "min_bytes_gbs": bytes_ / t / 1e9,
+                     "hbm_frac_of_measured": bytes_ / t / 1e9 / peaks["hbm_gbs"],
+                     "rel_residual_max": float((st[:, 0].sqrt() / st[:, 1].sqrt()).max())})
+        del a, l, out, work
+        torch.cuda.empty_cache()
+    return rows
+
+
 def _grid_summary(name, ms_step, shapes):
     """The reference leaderboard's ranking figure (AGENTS.md:58-64): the geometric mean of the
     per-call runtimes over the benchmark-grid entries, ours and the reference's published,
@@ -762,6 +816,8 @@ def main(argv=None):
     ap.add_argument("--shapes", action=argparse.BooleanOptionalAction, default=True,
                     help="also time the other benchmark shapes (N=1 only)")
     ap.add_argument("--big", action="store_true", help="include b1n32768 in --shapes")
+    ap.add_argument("--validate", action="store_true",
+                    help="also time the device-side checker (chol_validate_f32) (N=1 only)")
     ap.add_argument("--cyclic", action="store_true",
                     help="b1n32768 through the block-cyclic driver even on one GPU")
     ap.add_argument("--probe", default=None,

@@ -223,6 +223,29 @@ CHOL_API int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t n
                                      float alpha, float beta, int64_t diag_offset, int lower_only,
                                      int64_t col_block, int64_t col_stride, void* queue);
 
+/*
+ * Device-side check of a factor: the property gates of the reference's checker
+ * (finiteness, lower-triangular structure, positive diagonal, reconstruction residual
+ * against the FP32 input; reference AGENTS.md:47-50, harness gate
+ * cholesky/b4096n32/cholesky_b4096n32_modal.py:307-334), computed on the GPU so that a
+ * large factor needs no host copy. No kernel of the reference does this; the reference's
+ * checker runs in PyTorch. For each matrix m, with S the symmetric matrix the lower
+ * triangle of A defines and R = tril(L) tril(L)^T - S accumulated in FP64:
+ *   out[8m+0] = ||R||_F^2              out[8m+1] = ||S||_F^2
+ *   out[8m+2] = max_i sum_j |R_ij|     out[8m+3] = max_i sum_j |S_ij|
+ *   out[8m+4] = number of non-finite entries of L
+ *   out[8m+5] = number of entries strictly above the diagonal of L that are not +-0
+ *   out[8m+6] = number of diagonal entries of L that are not > 0
+ *   out[8m+7] = 0
+ * out: 8*batch doubles of device memory; work: chol_validate_work_bytes(batch, n) bytes of
+ * device memory (FP64 row sums). Both 8-byte aligned; both overwritten. Asynchronous on
+ * `queue`: read out after synchronising it. A non-zero upper part of L does not enter R;
+ * out[8m+5] reports it.
+ */
+CHOL_API size_t chol_validate_work_bytes(int64_t batch, int64_t n);
+CHOL_API int chol_validate_f32(const float* A, const float* L, int64_t batch, int64_t n,
+                               double* out, void* work, void* queue);
+
 #ifdef __cplusplus
 }
 #endif

@@ -149,13 +149,22 @@ def config_input(cfg: Config | str, device="cpu", batch: int | None = None):
     return covariance(b, cfg.n, cfg.param, cfg.seed, device)
 
 
+def generate_input(batch: int, n: int, seed: int, case_name: str | None = None,
+                   device="cpu") -> torch.Tensor:
+    """One seeded input (float32, contiguous) for any (batch, n): the structural case when
+    one is named, else the family the benchmark grid uses at this n (spectral with
+    lam_max 1e2 up to n = 32 and 1e3 up to n = 256, covariance with shift 1 up to n = 1024
+    and 0.5 above)."""
+    if case_name is not None:
+        return case(case_name, batch, n, seed, device)
+    if n <= 256:
+        return spectral(batch, n, 1e2 if n <= 32 else 1e3, seed, device)[0]
+    return covariance(batch, n, 1.0 if n <= 1024 else 0.5, seed, device)[0]
+
+
 def spec_input(shape: ShapeSpec, device="cpu") -> torch.Tensor:
     """The input of one of the reference's test shapes (float32, contiguous)."""
-    if shape.case is not None:
-        return case(shape.case, shape.batch, shape.n, shape.seed, device)
-    if shape.n <= 256:
-        return spectral(shape.batch, shape.n, 1e3, shape.seed, device)[0]
-    return covariance(shape.batch, shape.n, 1.0, shape.seed, device)[0]
+    return generate_input(shape.batch, shape.n, shape.seed, shape.case, device)
 
 
 def case(name: str, batch: int, n: int, seed: int, device="cpu") -> torch.Tensor:

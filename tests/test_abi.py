@@ -100,3 +100,37 @@ def test_info_check_without_entries():
     first = ctypes.c_int64(7)
     assert lib.chol_info_check(None, 0, None, ctypes.byref(first)) == _lib.CHOL_OK
     assert first.value == -1
+
+
+def test_validate_argument_checks():
+    """chol_validate_f32's host-side checks run before any device call."""
+    lib = _lib.load()
+    assert lib.chol_validate_work_bytes(3, 100) == 2 * 3 * 100 * 8
+    assert lib.chol_validate_work_bytes(0, 100) == 0
+    assert lib.chol_validate_f32(None, None, 0, 16, None, None, None) == _lib.CHOL_OK
+    assert lib.chol_validate_f32(None, None, -1, 16, None, None, None) == \
+        _lib.CHOL_ERR_INVALID_ARG
+    assert lib.chol_validate_f32(None, None, 2, 16, None, None, None) == \
+        _lib.CHOL_ERR_INVALID_ARG
+    buf = (ctypes.c_double * 64)()
+    p = ctypes.addressof(buf)
+    # a misaligned output pointer is rejected
+    assert lib.chol_validate_f32(ctypes.c_void_p(p), ctypes.c_void_p(p), 1, 4,
+                                 ctypes.c_void_p(p + 4), ctypes.c_void_p(p), None) == \
+        _lib.CHOL_ERR_INVALID_ARG
+
+
+def test_check_implementation_contract_on_the_host():
+    """The shape / dtype / device gates answer without a GPU; the residual gates need one
+    (no CPU fallback)."""
+    import torch
+
+    from linalg_kernels_b200.validate import check_implementation, validate
+
+    a = torch.eye(4).expand(2, 4, 4).contiguous()
+    assert check_implementation(a, a[:1]) == (False, "output shape (1, 4, 4) != input shape "
+                                                     "(2, 4, 4)")
+    assert check_implementation(a, a.double())[0] is False
+    assert check_implementation(a, None)[0] is False
+    with pytest.raises(TypeError, match="GPU"):
+        validate(a, a)

@@ -57,3 +57,13 @@ def test_test_shape_inputs_are_spd(spec):
     assert (info == 0).all()
     res = oracle.check_factor(a, l)
     assert res["ok"], res
+
+
+def test_generate_input_follows_the_grid_families():
+    """generate_input(batch, n, seed) gives the grid entry's own input at its shape."""
+    for name in ("b4096n32", "b256n128", "b16n512", "b2n2048"):
+        cfg = inputs.GRID[name]
+        b = min(cfg.batch, 2)
+        want, _ = inputs.config_input(cfg, batch=b)
+        got = inputs.generate_input(b, cfg.n, cfg.seed)
+        assert np.array_equal(got.numpy(), want.numpy()), name

@@ -440,7 +440,8 @@ def _roofline(args, cfg, per_step_ms, peaks, peak_kind, lib, pool, dev, dist):
         bytes_ = 8.0 * n * n * b
         achieved = bytes_ / t / 1e9
         peak = peaks["hbm_gbs"]
-        return {"bound": "hbm", "kernel": "small_potrf_kernel", "achieved": achieved,
+        kernel = "small_potrf_kernel" if n <= 64 else "mid_potrf_kernel"
+        return {"bound": "hbm", "kernel": kernel, "achieved": achieved,
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_kind": f"{peak_kind} hbm_gbs (burst copy)",
                 "traffic": NCU_TRAFFIC_BYTES.get(cfg.name),

@@ -71,7 +71,7 @@ CHOL_API int chol_prepare(int device);
 
 /*
  * Bytes of device workspace chol_potrf_batched_ws_f32 needs for (batch, n).
- * 0 when the chosen kernels need none (small n).
+ * 0 when the chosen kernels need none (n <= 128 with the default options).
  */
 CHOL_API size_t chol_workspace_bytes(int64_t batch, int64_t n);
 
@@ -106,7 +106,8 @@ CHOL_API int chol_potrf_batched_ws_f32(const float* A, float* L, int64_t batch, 
  * and info as usual, and the only scratch (the 64 x 64 inverse diagonal blocks of the
  * blocked path, 16 KiB per matrix with n > 64) comes from a fixed 4 MiB device array
  * inside the library, held on every GPU that loads the library until exit. Problems that
- * need more (batch > 256 when n > 64) return CHOL_ERR_SCRATCH_LIMIT; n <= 64 needs none.
+ * need more (batch > 256 when n > 128) return CHOL_ERR_SCRATCH_LIMIT; n <= 128 needs none
+ * (with the default options).
  * The first call on a device looks up the array's device address with that device
  * current; make that first call before any stream capture. All calls share the array:
  * calls that overlap on the GPU race and must be serialised by the caller.
@@ -151,6 +152,10 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   loading before they finish (it still completes after them); 0 = every call waits for
  *   the previous kernel on its queue before reading. */
 #define CHOL_OPT_OVERLAP_CALLS 7
+/*   CHOL_OPT_MID_KERNEL: 1 (default) = 64 < n <= 128 is factored by one launch with one CTA
+ *   per matrix held in shared memory, needing no workspace; 0 = the blocked schedule (the
+ *   workspace sizes then follow it: size workspaces after setting this). */
+#define CHOL_OPT_MID_KERNEL 8
 CHOL_API int chol_set_option(int option, int value);
 
 /*

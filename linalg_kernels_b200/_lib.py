@@ -32,6 +32,7 @@ CHOL_OPT_LOOKAHEAD = 4
 CHOL_OPT_CHAIN_SMS = 5
 CHOL_OPT_PANEL_INVERSE = 6
 CHOL_OPT_OVERLAP_CALLS = 7
+CHOL_OPT_MID_KERNEL = 8
 ENGINE_AUTO, ENGINE_FMA, ENGINE_TENSOR = 0, 1, 2
 
 _i64 = ctypes.c_int64

@@ -4,6 +4,7 @@
 // where the reference routes exact shapes to per-shape modules and sends everything else
 // to torch, this library plans every (batch, n) on the GPU:
 //   n <= 64   one launch of the warp-register kernel (chol_small.cu)
+//   n <= 128  one launch of the shared-memory kernel, one CTA per matrix (chol_mid.cu)
 //   n  > 64   right-looking blocked schedule, 64-wide diagonal blocks, outer panels of
 //             width NB, left-looking inside a panel and right-looking between panels:
 //               copy tril(A) -> L
@@ -89,7 +90,7 @@ bool overlaps_partially(const float* a, const float* b, int64_t count) {
 // the trailing GEMM loads instead of splitting in shared memory, and V = inv(L11) of the
 // panel's NB x NB diagonal block (NB x NB floats per matrix).
 size_t blocked_workspace_min(int64_t batch, int64_t n) {
-  if (n <= 64) return 0;
+  if (n <= 64 || use_mid(n)) return 0;
   const size_t tinv = size_t(batch) * kBlock * kBlock * sizeof(float);
   const size_t counters = (size_t(batch) * sizeof(unsigned) + 255) & ~size_t(255);
   return tinv + counters;
@@ -123,6 +124,7 @@ size_t blocked_diag_bytes(int64_t batch, int64_t n) {
          256;
 }
 size_t blocked_workspace(int64_t batch, int64_t n) {
+  if (use_mid(n)) return 0;
   return blocked_workspace_min(batch, n) + blocked_lo_bytes(batch, n) +
          blocked_inv_bytes(batch, n) + blocked_diag_bytes(batch, n);
 }
@@ -488,6 +490,7 @@ int check_common(const float* A, float* L, int64_t batch, int64_t n) {
 int potrf_impl(const float* A, float* L, int64_t batch, int64_t n, int* info, void* ws,
                size_t ws_bytes, cudaStream_t q) {
   if (n <= 64) return launch_small(A, L, batch, int(n), info, q);
+  if (use_mid(n)) return launch_mid(A, L, batch, int(n), info, q);
   if (ws == nullptr || ws_bytes < blocked_workspace_min(batch, n)) return CHOL_ERR_WORKSPACE;
   if (batch > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
   return run_blocked(A, L, batch, n, info, static_cast<float*>(ws), ws_bytes, q);
@@ -570,7 +573,7 @@ int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int
 
 int prepare_kernels(int /*device*/) {
   return (prepare_tc() == cudaSuccess && prepare_panel() == cudaSuccess &&
-          prepare_blocked() == cudaSuccess)
+          prepare_blocked() == cudaSuccess && prepare_mid() == cudaSuccess)
              ? CHOL_OK
              : CHOL_ERR_DEVICE;
 }
@@ -669,7 +672,7 @@ int chol_potrf_batched_f32(const float* A, float* L, int64_t batch, int64_t n, i
 
 int64_t chol_launch_count(int64_t batch, int64_t n) {
   if (batch <= 0 || n <= 0) return 0;
-  if (n <= 64) return 1;
+  if (n <= 64 || use_mid(n)) return 1;
   // the fused panel step runs when the tensor-core engine is allowed and rows are
   // 16-byte multiples (the usual case: n % 4 == 0)
   return blocked_launches(batch, n, use_fused(batch, n) && g_gemm_engine != 1 && n % 4 == 0);
@@ -694,6 +697,11 @@ int chol_set_option(int option, int value) {
   if (option == CHOL_OPT_CHAIN_SMS) {
     if (value < 1 || value > 120) return CHOL_ERR_INVALID_ARG;
     g_chain_sms = value;
+    return CHOL_OK;
+  }
+  if (option == CHOL_OPT_MID_KERNEL) {
+    if (value < 0 || value > 1) return CHOL_ERR_INVALID_ARG;
+    g_mid_kernel = value;
     return CHOL_OK;
   }
   if (option == CHOL_OPT_OVERLAP_CALLS) {

@@ -159,6 +159,12 @@ int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int
 cudaError_t prepare_small();
 int prepare_kernels(int device);
 int launch_small(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q);
+// 64 < n <= 128: one CTA per matrix in shared memory (chol_mid.cu), unless
+// CHOL_OPT_MID_KERNEL is 0.
+extern int g_mid_kernel;
+bool use_mid(int64_t n);
+cudaError_t prepare_mid();
+int launch_mid(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q);
 // Overlap of back-to-back independent small calls on one queue (on by default).
 void set_overlap_small(int on);
 int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaStream_t q,

@@ -6,7 +6,7 @@
 // acceptable. chol_potrf_batched_f32 grows a cached workspace with cudaMalloc, and
 // chol_potrf_batched_ws_f32 needs the caller to allocate one. This entry point instead
 // takes the only scratch the factorisation needs (the inverse of each 64 x 64 diagonal
-// block of the blocked path, 16 KiB per matrix with n > 64, and a 4-byte arrival counter per
+// block of the blocked path, 16 KiB per matrix with n > 128, and a 4-byte arrival counter per
 // matrix) from one fixed file-scope device array, g_noalloc_scratch, of kNoAllocScratchBytes
 // (4 MiB + 64 KiB). Every GPU that loads
 // the library holds that array until the process exits.
@@ -28,7 +28,7 @@
 namespace chol {
 namespace {
 
-// 4 MiB of inverse blocks + 64 KiB of per-matrix counters: 256 matrices with n > 64
+// 4 MiB of inverse blocks + 64 KiB of per-matrix counters: 256 matrices with n > 128
 constexpr size_t kNoAllocScratchBytes = (size_t(4) << 20) + (size_t(64) << 10);
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];

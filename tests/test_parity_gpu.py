@@ -176,7 +176,7 @@ def _abi_call(a, l, batch, n):
                                       ctypes.c_void_p(_lib.current_queue(torch.device(DEV))))
 
 
-@pytest.mark.parametrize("n", [32, 64, 200])
+@pytest.mark.parametrize("n", [32, 64, 100, 200])
 def test_abi_in_place_and_canaries(n):
     """Library-managed workspace entry point; A == L in place; canaries around L."""
     a, cond = inputs.spectral(3, n, 50.0, 11 + n)
@@ -273,6 +273,42 @@ def test_single_panel_sizes(batch, n, lam, panel_inverse):
         _check_input(a, cond)
     finally:
         lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)
+
+
+# 64 < n <= 128: the shared-memory kernel (one CTA per matrix) against the oracle, and the
+# blocked schedule (CHOL_OPT_MID_KERNEL = 0, through the library-workspace C entry) for the
+# same inputs within the same bounds
+@pytest.mark.parametrize("batch,n", [(256, 128), (7, 65), (33, 100), (5, 127), (600, 96)])
+def test_mid_kernel_sizes(batch, n):
+    lib = _lib.load()
+    a, cond = inputs.spectral(batch, n, 1e3, 8500 + n)
+    l_or, _ = oracle.potrf(a.numpy())
+    a_dev = a.to(DEV)
+    l_mid = custom_kernel(a_dev)
+    lib.chol_set_option(_lib.CHOL_OPT_MID_KERNEL, 0)
+    try:
+        l_blk = torch.empty_like(a_dev)
+        assert _abi_call(a_dev.data_ptr(), l_blk.data_ptr(), batch, n) == _lib.CHOL_OK
+        torch.cuda.synchronize()
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_MID_KERNEL, 1)
+    for name, l in (("mid", l_mid), ("blocked", l_blk)):
+        res = oracle.check_factor(a.numpy(), l.cpu().numpy(), l_ref=l_or, cond=cond.numpy())
+        assert res["ok"], (name, batch, n, res)
+
+
+def test_mid_kernel_not_spd_info():
+    """info from the shared-memory kernel: the first failing column, as LAPACK reports it
+    (in the first panel, a later panel and the last column)."""
+    a, _ = inputs.spectral(5, 100, 10.0, 98, device=DEV)
+    a = a.clone()
+    a[1, 10, 10] = -1.0
+    a[2, 70, 70] = -5.0
+    a[4, 99, 99] = -3.0
+    l, info = cholesky_ex(a)
+    want = torch.linalg.cholesky_ex(a.cpu()).info
+    assert torch.equal(info.cpu(), want), (info.cpu(), want)
+    assert want.tolist()[0] == 0 and want.tolist()[3] == 0
 
 
 def test_single_panel_not_spd_info():

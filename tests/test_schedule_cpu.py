@@ -1,7 +1,8 @@
 """CPU: the host side of the schedule choice, through the C ABI without a GPU.
 
 chol_launch_count and chol_workspace_bytes are pure host logic; they follow the schedules
-the blocked path picks: one small-kernel launch for n <= 64; for one panel, the whole matrix
+the blocked path picks: one small-kernel launch for n <= 64, one shared-memory-kernel launch
+for n <= 128; for one panel, the whole matrix
 in one diagonal-block launch while batch * n^3 is small, else the 64-wide chain (a zero fill,
 then per 64 columns a factor, a left-looking update and a solve); for several 512-wide
 panels, per panel the diagonal block, the solve GEMM, the split and the trailing update.
@@ -32,6 +33,24 @@ ROOT = Path(__file__).resolve().parents[1]
 ])
 def test_launch_counts_follow_the_schedule(batch, n, launches):
     assert int(_lib.load().chol_launch_count(batch, n)) == launches
+
+
+def test_mid_sizes_take_one_launch_and_no_workspace():
+    """64 < n <= 128: one launch of the shared-memory kernel, no workspace; with
+    CHOL_OPT_MID_KERNEL = 0 the blocked schedule (and its workspace) comes back."""
+    lib = _lib.load()
+    for b, n in ((256, 128), (7, 65), (33, 100)):
+        assert int(lib.chol_launch_count(b, n)) == 1
+        assert int(lib.chol_workspace_bytes(b, n)) == 0
+    assert lib.chol_set_option(_lib.CHOL_OPT_MID_KERNEL, 2) == _lib.CHOL_ERR_INVALID_ARG
+    assert lib.chol_set_option(_lib.CHOL_OPT_MID_KERNEL, 0) == _lib.CHOL_OK
+    try:
+        assert int(lib.chol_launch_count(256, 128)) == 2    # diagonal-block launch + copy
+        assert int(lib.chol_workspace_bytes(256, 128)) > 0
+        assert int(lib.chol_launch_count(7, 100)) > 1
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_MID_KERNEL, 1)
+    assert int(lib.chol_launch_count(256, 130)) > 1           # past the mid range
 
 
 def test_workspace_regions():

@@ -6,9 +6,10 @@
 // for that shape.
 //
 // Per matrix (256 threads, 8 warps):
-//   load      the lower triangle of A into shared memory, row-major with an odd row
-//             stride (n | 1 floats), so that a column read by 32 consecutive rows hits
-//             32 distinct banks; warp w reads rows w, w + 8, ... (coalesced).
+//   load      the lower triangle of A into shared memory by cp.async (all copies in
+//             flight at once, one wait), row-major with an odd row stride (n | 1 floats),
+//             so that a column read by 32 consecutive rows hits 32 distinct banks; warp w
+//             copies rows w, w + 8, ... (coalesced).
 //   per panel k0 = 0, 32, ...:
 //     factor  warp 0, lane i holding row k0 + i of the 32 x 32 diagonal block in
 //             registers: per column j the pivot comes from lane j by shuffle, r = rsqrt(d),
@@ -18,8 +19,9 @@
 //     solve   one thread per row below the block: x = a L_D^{-T} by forward substitution
 //             (x_j = (a_j - sum_{i<j} x_i L_D[j][i]) r_j) in chunks of 8 columns, the L_D
 //             entries read as shared-memory broadcasts.
-//     update  the lower triangle of the trailing rows and columns minus X X^T, K = 32, in
-//             4 x 4 register blocks over the lower block triangle.
+//     update  the lower triangle of the trailing rows and columns minus X X^T, K = 32,
+//             thread (tx, ty) of a 16 x 16 grid owning the rows ty + 16 i and columns
+//             tx + 16 c (conflict-free shared-memory reads).
 //   store     L row by row with zeros above the diagonal (coalesced); info = the first
 //             diagonal entry that is not > 0 (a non-positive pivot makes every later pivot
 //             NaN, so the first one is LAPACK's info).
@@ -82,6 +84,7 @@ __device__ __forceinline__ void mid_solve_row(float* As, int ld, int k0, int w, 
 #pragma unroll
     for (int c = 0; c < 8; ++c) x[c] = (q + c < w) ? row[q + c] : 0.f;
     const float* lq = As + (k0 + q) * ld + k0;  // L_D[q + c][i] at lq[c * ld + i]
+#pragma unroll 4
     for (int i = 0; i < q; ++i) {
       const float xi = row[i];
 #pragma unroll
@@ -104,51 +107,46 @@ __device__ __forceinline__ void mid_solve_row(float* As, int ld, int k0, int w, 
 }
 
 // All threads: the lower triangle of rows / columns [k1, n) minus X X^T, where X is
-// columns [k0, k0 + w) of those rows.
+// columns [k0, k0 + w) of those rows. Thread (tx, ty) owns rows k1 + ty + 16 i and columns
+// k1 + tx + 16 c with c <= i < 6 (for c > i every entry lies above the diagonal): per k a
+// warp reads 2 rows (broadcasts) and 16 consecutive rows n | 1 floats apart (distinct
+// banks), so the reads are conflict-free.
 __device__ __forceinline__ void mid_update(float* As, int ld, int n, int k0, int w, int k1,
                                            int tid) {
-  const int mrows = n - k1;
-  const int mb = (mrows + 3) >> 2;
-  const int nblk = mb * (mb + 1) / 2;
-  for (int b = tid; b < nblk; b += kMidThreads) {
-    int bi = int((sqrtf(8.f * float(b) + 1.f) - 1.f) * 0.5f);
-    while (bi * (bi + 1) / 2 > b) --bi;
-    while ((bi + 1) * (bi + 2) / 2 <= b) ++bi;
-    const int bj = b - bi * (bi + 1) / 2;
-    const int r0 = k1 + 4 * bi, c0 = k1 + 4 * bj;
-    int ro[4], co[4];
+  const int tx = tid & 15, ty = tid >> 4;
+  const int tiles = (n - k1 + 15) >> 4;  // <= 6
+  int ro[6], co[6];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      // rows past n read row n - 1 (in bounds); their results are not written
-      ro[i] = min(r0 + i, n - 1) * ld + k0;
-      co[i] = min(c0 + i, n - 1) * ld + k0;
-    }
-    float acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[i][c] = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < w; ++j) {
-      float xr[4], xc[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        xr[i] = As[ro[i] + j];
-        xc[i] = As[co[i] + j];
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[i][c] = fmaf(xr[i], xc[c], acc[i][c]);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int r = r0 + i, col = c0 + c;
-        if (r < n && col <= r) As[r * ld + col] -= acc[i][c];
-      }
+  for (int i = 0; i < 6; ++i) {
+    // rows past n read row n - 1 (in bounds); their results are not written
+    ro[i] = min(k1 + ty + 16 * i, n - 1) * ld + k0;
+    co[i] = min(k1 + tx + 16 * i, n - 1) * ld + k0;
   }
+  float acc[6][6];
+#pragma unroll
+  for (int i = 0; i < 6; ++i)
+#pragma unroll
+    for (int c = 0; c <= i; ++c) acc[i][c] = 0.f;
+#pragma unroll 4
+  for (int j = 0; j < w; ++j) {
+    float xr[6], xc[6];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      xr[i] = i < tiles ? As[ro[i] + j] : 0.f;
+      xc[i] = i < tiles ? As[co[i] + j] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 6; ++i)
+#pragma unroll
+      for (int c = 0; c <= i; ++c) acc[i][c] = fmaf(xr[i], xc[c], acc[i][c]);
+  }
+#pragma unroll
+  for (int i = 0; i < 6; ++i)
+#pragma unroll
+    for (int c = 0; c <= i; ++c) {
+      const int r = k1 + ty + 16 * i, col = k1 + tx + 16 * c;
+      if (i < tiles && r < n && col <= r) As[r * ld + col] -= acc[i][c];
+    }
 }
 
 __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
@@ -163,7 +161,8 @@ __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
     const float* Am = A + m * int64_t(n) * n;
     float* Lm = L + m * int64_t(n) * n;
     for (int r = warp; r < n; r += kMidThreads / 32)
-      for (int c = lane; c <= r; c += 32) As[r * ld + c] = Am[int64_t(r) * n + c];
+      for (int c = lane; c <= r; c += 32) cp_async4(&As[r * ld + c], Am + int64_t(r) * n + c);
+    cp_async_wait_all();
     __syncthreads();
     for (int k0 = 0; k0 < n; k0 += 32) {
       const int w = min(32, n - k0);

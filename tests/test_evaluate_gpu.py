@@ -23,4 +23,6 @@ def test_benchmark_loop_on_small_grid_entries(index):
     r = evaluate.run_benchmark(case, True, 5, 1e9)
     assert isinstance(r, evaluate.Stats), r
     assert 3 <= r.runs <= 5
-    assert 0 < r.best <= r.mean <= r.worst < 1e6  # ns per call
+    # ns per call; the first window also pays for its fresh outputs' allocations (in the
+    # reference's evaluator too), so only the best window is bounded
+    assert 0 < r.best <= r.mean <= r.worst and r.best < 1e6

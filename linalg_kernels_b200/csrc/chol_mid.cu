@@ -25,7 +25,8 @@
 //   store     L row by row with zeros above the diagonal (coalesced); info = the first
 //             diagonal entry that is not > 0 (a non-positive pivot makes every later pivot
 //             NaN, so the first one is LAPACK's info).
-// Shared memory: n (n | 1) floats (66 KB at n = 128): 3 CTAs per SM. No workspace, no
+// Shared memory: n (n | 1) floats (66 KB at n = 128); 2 CTAs per SM (the register budget
+// of 128 per thread lets the factor keep its shuffles in flight). No workspace, no
 // waits on other CTAs. A == L (in place) is allowed: a CTA reads its whole matrix before
 // it writes any of it.
 #include "chol_common.cuh"
@@ -35,7 +36,7 @@ namespace {
 
 constexpr int kMidMax = 128;
 constexpr int kMidThreads = 256;
-constexpr int kMidCtasPerSm = 3;
+constexpr int kMidCtasPerSm = 2;
 
 __device__ __forceinline__ float mid_rsqrt(float x) {
   float y;
@@ -56,13 +57,12 @@ __device__ __forceinline__ void mid_factor_diag(float* As, int ld, int k0, int w
     if (j < w) {
       const float d = __shfl_sync(0xffffffffu, a[j], j);
       const float r = mid_rsqrt(d);
-      if (lane == j) a[j] = d * r;
-      else if (lane > j) a[j] *= r;
+      a[j] = lane == j ? d * r : (lane > j ? a[j] * r : a[j]);
       if (lane == 0) rdg[k0 + j] = r;
 #pragma unroll
       for (int c = j + 1; c < 32; ++c) {
         const float lc = __shfl_sync(0xffffffffu, a[j], c);
-        if (c <= lane) a[c] = fmaf(-a[j], lc, a[c]);
+        a[c] = c <= lane ? fmaf(-a[j], lc, a[c]) : a[c];
       }
     }
   }

@@ -92,12 +92,17 @@ def _factor(data: torch.Tensor, want_info: bool):
 
 
 def _launch(lib, data, out, info, batch, n, dev):
-    need = _workspace_bytes(lib, batch, n)
-    ws = torch.empty(need, dtype=torch.uint8, device=data.device) if need else None
-    status = _lib.potrf_ws(
-        data.data_ptr(), out.data_ptr(), batch, n,
-        info.data_ptr() if info is not None else 0,
-        ws.data_ptr() if ws is not None else 0, need, _lib.current_queue(dev))
+    for attempt in range(2):
+        need = _workspace_bytes(lib, batch, n)
+        ws = torch.empty(need, dtype=torch.uint8, device=data.device) if need else None
+        status = _lib.potrf_ws(
+            data.data_ptr(), out.data_ptr(), batch, n,
+            info.data_ptr() if info is not None else 0,
+            ws.data_ptr() if ws is not None else 0, need, _lib.current_queue(dev))
+        if status != _lib.CHOL_ERR_WORKSPACE or attempt:
+            break
+        # a schedule option changed since the size was cached: ask the library again
+        _ws_bytes.pop((batch, n), None)
     if status:
         _lib.check(status, "chol_potrf_batched_ws_f32")
     return out, info

@@ -341,6 +341,8 @@ def run_ours(args, dist: Dist):
     # end to end through the C ABI: pinned host in -> device -> factor -> pinned host out
     e2e = _e2e(args, cfg, pool, lib, dev, dist)
 
+    from_root = _from_root(args, cfg, dev, dist) if dist.world > 1 and args.from_root else None
+
     cpu = None
     if dist.world == 1 and not args.no_cpu_baseline:
         cpu = _cpu_reference_rate(cfg, pool[0].cpu(), budget_s=args.cpu_budget)
@@ -379,6 +381,8 @@ def run_ours(args, dist: Dist):
         line["grid"] = _grid_summary(cfg.name, ms_step, shapes)
     if validator is not None:
         line["validator"] = validator
+    if from_root is not None:
+        line["e2e_from_root"] = from_root
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -713,6 +717,46 @@ def _validator_timing(dev, peaks, peak_kind, lib, names=("b1024n64", "b640n512",
     return rows
 
 
+def _from_root(args, cfg, dev, dist):
+    """Batch sharding end to end from one GPU: the global batch (world x batch matrices of
+    the config) sits on rank 0's GPU; each step, factor_batch_sharded sends every rank its
+    slice by NCCL point-to-point, each rank factors it, and the factors come back to rank 0.
+    The same input every step; CUDA events per rank around K steps, maximum over ranks."""
+    from linalg_kernels_b200 import inputs
+    from linalg_kernels_b200.distributed import factor_batch_sharded
+
+    b, n = cfg.batch, cfg.n
+    total = b * dist.world
+    a = None
+    if dist.rank == 0:
+        c = inputs.Config(cfg.name, total, n, cfg.family, cfg.param, cfg.seed)
+        a, _ = inputs.config_input(c, device=dev)
+
+    def step():
+        factor_batch_sharded(a, total, n, dist.pg, root=0)
+
+    steps = max(3, min(args.steps, 50))
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1)) / steps
+    moved = 2.0 * (total - b) * n * n * 4  # slices out and factors back (rank 0's own stays)
+    return {"value": total / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms,
+            "global_batch": total, "steps": steps, "nvlink_bytes_per_step": moved,
+            "path": "input on rank 0's GPU; slices out and factors back by NCCL "
+                    "point-to-point (factor_batch_sharded)"}
+
+
 def _grid_summary(name, ms_step, shapes):
     """The reference leaderboard's ranking figure (AGENTS.md:58-64): the geometric mean of the
     per-call runtimes over the benchmark-grid entries, ours and the reference's published,
@@ -817,6 +861,9 @@ def main(argv=None):
     ap.add_argument("--shapes", action=argparse.BooleanOptionalAction, default=True,
                     help="also time the other benchmark shapes (N=1 only)")
     ap.add_argument("--big", action="store_true", help="include b1n32768 in --shapes")
+    ap.add_argument("--from-root", action="store_true",
+                    help="N>1: also time batch sharding end to end from rank 0's GPU "
+                         "(NCCL point-to-point out and back)")
     ap.add_argument("--validate", action="store_true",
                     help="also time the device-side checker (chol_validate_f32) (N=1 only)")
     ap.add_argument("--cyclic", action="store_true",

@@ -36,7 +36,7 @@ import torch
 from . import _lib
 
 __all__ = ["CyclicLayout", "CudaOps", "factor_block_cyclic", "scatter_block_cyclic",
-           "gather_block_cyclic"]
+           "gather_block_cyclic", "batch_slices", "factor_batch_sharded"]
 
 
 @dataclass(frozen=True)
@@ -228,3 +228,70 @@ def _global_rank(pg, group, r):
     if group is None:
         return r
     return pg.get_global_rank(group, r)
+
+
+# --------------------------------------------------------------------------------------
+# batches of independent matrices (M1) from one GPU
+# --------------------------------------------------------------------------------------
+def batch_slices(batch: int, world: int) -> list[tuple[int, int]]:
+    """(offset, count) of each rank's contiguous slice of the batch; the first
+    ``batch % world`` ranks take one matrix more."""
+    base, extra = divmod(batch, world)
+    out, off = [], 0
+    for r in range(world):
+        c = base + (1 if r < extra else 0)
+        out.append((off, c))
+        off += c
+    return out
+
+
+def _p2p(pg, ops):
+    """Start a group of point-to-point transfers (none for an empty list)."""
+    return pg.batch_isend_irecv(ops) if ops else []
+
+
+def factor_batch_sharded(a: torch.Tensor | None, batch: int, n: int, pg, factor=None,
+                         root: int = 0, device=None) -> torch.Tensor | None:
+    """Batched factorisation spread over the ranks when the whole batch lives on one GPU.
+
+    ``a`` is the contiguous ``(batch, n, n)`` input on the root rank's device, and None on
+    the other ranks. The root sends each rank its contiguous slice of matrices by
+    point-to-point transfers (NCCL over NVLink on GPUs). Every rank factors its slice with
+    ``factor`` (``custom_kernel`` by default) and sends the factor back. The root returns
+    the ``(batch, n, n)`` factor and the other ranks return None. The matrices are
+    independent, so the two transfers are the only communication, and the root's own slice
+    never moves. Every rank calls this with the same ``batch``, ``n`` and ``root``. Each
+    rank needs at least one matrix: with NCCL, the first point-to-point call of a group
+    must include every rank. ``device`` is where the non-root ranks receive (default: the
+    current CUDA device)."""
+    world, rank = pg.get_world_size(), pg.get_rank()
+    if batch < world:
+        raise ValueError(f"batch {batch} < {world} ranks: every rank needs a matrix")
+    if factor is None:
+        from .cholesky import custom_kernel as factor
+    sl = batch_slices(batch, world)
+    off, cnt = sl[rank]
+    if rank == root:
+        if a is None or tuple(a.shape) != (batch, n, n) or not a.is_contiguous():
+            raise ValueError("the root needs the contiguous (batch, n, n) input")
+        sends = [pg.P2POp(pg.isend, a[o:o + c], r) for r, (o, c) in enumerate(sl) if r != root]
+        for w in _p2p(pg, sends):
+            w.wait()
+        mine = a[off:off + cnt]
+        l_mine = factor(mine)
+        out = torch.empty(batch, n, n, dtype=a.dtype, device=a.device)
+        recvs = [pg.P2POp(pg.irecv, out[o:o + c], r) for r, (o, c) in enumerate(sl)
+                 if r != root]
+        reqs = _p2p(pg, recvs)
+        out[off:off + cnt].copy_(l_mine)
+        for w in reqs:
+            w.wait()
+        return out
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    mine = torch.empty(cnt, n, n, dtype=torch.float32, device=dev)
+    for w in _p2p(pg, [pg.P2POp(pg.irecv, mine, root)]):
+        w.wait()
+    l_mine = factor(mine).contiguous()
+    for w in _p2p(pg, [pg.P2POp(pg.isend, l_mine, root)]):
+        w.wait()
+    return None

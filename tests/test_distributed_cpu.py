@@ -118,3 +118,89 @@ def test_scatter_gather_roundtrip():
     a = torch.tril(_matrix(n, 3))
     parts = [scatter_block_cyclic(a, CyclicLayout(n, world, r, bs)) for r in range(world)]
     assert torch.equal(gather_block_cyclic(parts, n, world, bs), a)
+
+
+# --------------------------------------------------------------------------------------
+# batches of independent matrices from one root (factor_batch_sharded)
+# --------------------------------------------------------------------------------------
+def _cpu_factor(x):
+    return torch.linalg.cholesky_ex(x).L  # stand-in for custom_kernel (test only)
+
+
+def _batch(batch, n, seed):
+    return torch.stack([_matrix(n, seed + i) for i in range(batch)])
+
+
+def _sharded_worker(rank, world, port, batch, n, root, out_dir):
+    import torch.distributed as dist
+
+    from linalg_kernels_b200.distributed import factor_batch_sharded
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        a = _batch(batch, n, 40) if rank == root else None
+        seen = []
+
+        def factor(x):
+            seen.append(x.shape[0])
+            return _cpu_factor(x)
+
+        l = factor_batch_sharded(a, batch, n, dist, factor=factor, root=root,
+                                 device=torch.device("cpu"))
+        torch.save({"l": l, "seen": seen}, os.path.join(out_dir, f"r{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_batch_slices():
+    from linalg_kernels_b200.distributed import batch_slices
+
+    assert batch_slices(10, 4) == [(0, 3), (3, 3), (6, 2), (8, 2)]
+    assert batch_slices(8, 2) == [(0, 4), (4, 4)]
+    assert sum(c for _, c in batch_slices(1024, 8)) == 1024
+
+
+@pytest.mark.parametrize("world,batch,root", [(2, 5, 0), (3, 7, 1), (2, 2, 0)])
+def test_batch_sharded_gloo_matches_one_rank(tmp_path, world, batch, root):
+    """Every rank factors its own contiguous slice; the root gets back the whole factor,
+    equal to the stand-in over the whole batch, and the other ranks get None."""
+    from linalg_kernels_b200.distributed import batch_slices
+
+    n = 24
+    port = _free_port()
+    mp.spawn(_sharded_worker, args=(world, port, batch, n, root, str(tmp_path)), nprocs=world,
+             join=True)
+    res = [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
+    want = _cpu_factor(_batch(batch, n, 40))
+    assert torch.equal(res[root]["l"], want)
+    for r in range(world):
+        assert res[r]["seen"] == [batch_slices(batch, world)[r][1]]
+        if r != root:
+            assert res[r]["l"] is None
+
+
+def test_batch_sharded_single_rank_and_argument_checks():
+    from linalg_kernels_b200.distributed import factor_batch_sharded
+
+    class OneRank:
+        def get_world_size(self):
+            return 1
+
+        def get_rank(self):
+            return 0
+
+    a = _batch(3, 16, 7)
+    assert torch.equal(factor_batch_sharded(a, 3, 16, OneRank(), factor=_cpu_factor),
+                       _cpu_factor(a))
+    with pytest.raises(ValueError):
+        factor_batch_sharded(None, 3, 16, OneRank(), factor=_cpu_factor)
+
+    class TwoRanks(OneRank):
+        def get_world_size(self):
+            return 2
+
+    with pytest.raises(ValueError, match="every rank"):
+        factor_batch_sharded(a[:1], 1, 16, TwoRanks(), factor=_cpu_factor)

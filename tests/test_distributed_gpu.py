@@ -92,6 +92,56 @@ def test_cyclic_two_ranks_nccl(tmp_path):
     assert res["ok"], res
 
 
+def _sharded_nccl_worker(rank, world, port, batch, n, out_dir):
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    from linalg_kernels_b200.distributed import factor_batch_sharded
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        a = None
+        if rank == 0:
+            a, _ = inputs.spectral(batch, n, 100.0, 4343, device="cuda:0")
+        l = factor_batch_sharded(a, batch, n, dist, root=0)
+        torch.cuda.synchronize()
+        if rank == 0:
+            torch.save(l.cpu(), os.path.join(out_dir, "l.pt"))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_batch_sharded_two_ranks_nccl(tmp_path):
+    """A batch on cuda:0 factored by two ranks (slices out and factors back over NCCL)
+    equals the one-GPU factor bitwise: the same kernel on the same matrices."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    from linalg_kernels_b200.cholesky import custom_kernel
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    batch, n = 9, 48
+    mp.spawn(_sharded_nccl_worker, args=(2, port, batch, n, str(tmp_path)), nprocs=2,
+             join=True)
+    l = torch.load(tmp_path / "l.pt")
+    a, _ = inputs.spectral(batch, n, 100.0, 4343, device=DEV)
+    want = torch.cat([custom_kernel(a[:5]), custom_kernel(a[5:])]).cpu()
+    assert torch.equal(l, want)
+
+
 @pytest.mark.parametrize("world,nblk", [(1, 3), (2, 3), (3, 2)])
 def test_cyclic_gemm_matches_per_block(world, nblk):
     """chol_gemm_nt_cyclic_f32 (one launch over cyclically stored blocks) equals the same

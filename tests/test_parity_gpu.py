@@ -134,6 +134,27 @@ def test_baseline_config_n16384():
     _check_full_config("b1n16384")
 
 
+def test_baseline_config_n32768():
+    """b1n32768 (4 GiB): the residual gates from the device checker (an FP64 product would
+    need several 8 GiB buffers), and the elementwise bound against the reference path on
+    the GPU (torch.linalg.cholesky_ex)."""
+    from linalg_kernels_b200.validate import check_implementation, validate
+
+    a, cond = inputs.config_input("b1n32768", device=DEV)
+    a_before = a.clone()
+    l = custom_kernel(a)
+    torch.cuda.synchronize()
+    assert torch.equal(a, a_before), "input was modified"
+    del a_before
+    good, msg = check_implementation(a, l)
+    assert good, msg
+    assert validate(a, l)["rel_residual"].item() <= oracle.REL_RESIDUAL_TOL
+    l_ref = torch.linalg.cholesky_ex(a, check_errors=False).L
+    diff = (l - l_ref).abs().max().item()
+    bound = float(cond[0]) * a.shape[-1] * oracle.EPS32 * l_ref.abs().max().item()
+    assert diff <= bound, (diff, bound)
+
+
 # the rest of the reference's benchmark grid (AGENTS.md:66-81), full size
 @pytest.mark.parametrize("name", [k for k in inputs.GRID if k not in inputs.CONFIGS])
 def test_benchmark_grid_full_size(name):

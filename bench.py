@@ -183,11 +183,28 @@ class ClockSampler:
 # --------------------------------------------------------------------------------------
 # helpers
 # --------------------------------------------------------------------------------------
+def _pool_count(cfg, max_inputs: int) -> int:
+    in_bytes = cfg.batch * cfg.n * cfg.n * 4
+    return 1 if in_bytes >= 2 * L2_BYTES else min(max_inputs, math.ceil(2 * L2_BYTES / in_bytes))
+
+
+def _config(cfg, world: int) -> dict:
+    """The workload description both arms print (identical for the same config and N)."""
+    count = _pool_count(cfg, 32)
+    in_bytes = cfg.batch * cfg.n * cfg.n * 4
+    return {"workload": cfg.name, "batch": cfg.batch, "n": cfg.n,
+            "global_batch": cfg.batch * world, "family": cfg.family, "param": cfg.param,
+            "seed": cfg.seed,
+            "parallelism": f"batch-sharded x{world} (independent matrices, no collective)",
+            "l2": f"GPU arm: inputs rotate over {count} distinct (batch, n, n) tensors "
+                  f"({count * in_bytes / 2**20:.0f} MiB > 2x L2)"}
+
+
 def _pool(cfg, device, rank: int, max_inputs: int):
     from linalg_kernels_b200 import inputs
 
     in_bytes = cfg.batch * cfg.n * cfg.n * 4
-    count = 1 if in_bytes >= 2 * L2_BYTES else min(max_inputs, math.ceil(2 * L2_BYTES / in_bytes))
+    count = _pool_count(cfg, max_inputs)
     pool = []
     cond = None
     for i in range(count):
@@ -222,6 +239,24 @@ def _time_steps(fn, pool, steps: int, warmup: int, dist: Dist):
     return start.elapsed_time(end), None
 
 
+def _cpu_sample_size(cfg, a_host: torch.Tensor, budget_s: float) -> int:
+    """Matrices per CPU step: the whole batch for n <= 1024 (every such config takes well under
+    a second on the host cores), else as many as fit the budget (at least one), sized from a
+    warm call."""
+    from oracle import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample_b = a_host.shape[0]
+    if cfg.n <= 1024:
+        return sample_b
+    x = a_host[:1]
+    oracle.reference_factor(x)  # warm: MKL's threads and buffers
+    t0 = time.perf_counter()
+    oracle.reference_factor(x)
+    one = max(time.perf_counter() - t0, 1e-6)
+    return sample_b if one * sample_b <= budget_s else max(1, int(budget_s / one))
+
+
 def _cpu_reference_rate(cfg, a_host: torch.Tensor, budget_s: float) -> dict:
     """The reference's CPU path (submission.py:7 on CPU tensors: LAPACK via MKL) on a
     bounded sample of the workload; all host threads."""
@@ -230,14 +265,7 @@ def _cpu_reference_rate(cfg, a_host: torch.Tensor, budget_s: float) -> dict:
     torch.set_num_threads(os.cpu_count() or 1)
     threads = torch.get_num_threads()
     per_mat = cfg.n ** 3 / 3.0
-    # sample: whole batch if it is cheap, else a prefix of the batch (at least 1 matrix)
-    sample_b = a_host.shape[0]
-    x = a_host[:1]
-    t0 = time.perf_counter()
-    oracle.reference_factor(x)
-    one = max(time.perf_counter() - t0, 1e-6)
-    if one * sample_b > budget_s:
-        sample_b = max(1, int(budget_s / one))
+    sample_b = _cpu_sample_size(cfg, a_host, budget_s)
     x = a_host[:sample_b].contiguous()
     oracle.reference_factor(x)  # warm
     reps, times = 0, []
@@ -283,12 +311,12 @@ def run_reference(args, dist: Dist):
         del a
     else:
         a_host, _ = inputs.config_input(cfg, device="cpu", batch=min(cfg.batch, 64))
-    # each step: a bounded sample of the workload (about 1 s of CPU work at most)
-    base = _cpu_reference_rate(cfg, a_host, budget_s=1.0)
-    sample_b = int(base["sample"].split(" ")[0])
+    # each step: the whole batch for n <= 1024, else a bounded sample (about 1 s of CPU work)
+    sample_b = _cpu_sample_size(cfg, a_host, budget_s=1.0)
     x = a_host[:sample_b].contiguous()
     from oracle import oracle
 
+    threads = torch.get_num_threads()
     for _ in range(args.warmup):
         oracle.reference_factor(x)
     t0 = time.perf_counter()
@@ -296,17 +324,18 @@ def run_reference(args, dist: Dist):
         oracle.reference_factor(x)
     dt = time.perf_counter() - t0
     value = sample_b * args.steps / dt
+    sample = (f"{sample_b} of {cfg.batch} matrices of n={cfg.n} per step, "
+              f"torch.linalg.cholesky_ex on CPU (MKL LAPACK spotrf)")
     line = {
         "impl": "reference", "metric": "matrices/s", "value": value, "unit": "matrices/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "tflops": value * cfg.n ** 3 / 3.0 / 1e12,
-        "config": {"workload": cfg.name, "batch": cfg.batch, "n": cfg.n,
-                   "family": cfg.family, "seed": cfg.seed,
-                   "step": f"torch.linalg.cholesky_ex on {sample_b} host matrices"},
-        "cpu_baseline": {"value": value, "unit": "matrices/s", "cores": base["cores"],
-                         "kind": "reference", "sample": base["sample"], "cpu": base["cpu"]},
+        "config": _config(cfg, args.gpus),
+        "reference_step": sample,
+        "cpu_baseline": {"value": value, "unit": "matrices/s", "cores": threads,
+                         "kind": "reference", "sample": sample, "cpu": _cpu_model()},
         "e2e": {"value": value, "unit": "matrices/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -340,16 +369,20 @@ def run_ours(args, dist: Dist):
 
     # end to end through the C ABI: pinned host in -> device -> factor -> pinned host out
     e2e = _e2e(args, cfg, pool, lib, dev, dist)
-
-    from_root = _from_root(args, cfg, dev, dist) if dist.world > 1 and args.from_root else None
+    a_host = pool[0].cpu() if dist.world == 1 and not args.no_cpu_baseline else None
+    del pool
+    torch.cuda.empty_cache()
 
     cpu = None
     if dist.world == 1 and not args.no_cpu_baseline:
-        cpu = _cpu_reference_rate(cfg, pool[0].cpu(), budget_s=args.cpu_budget)
+        cpu = _cpu_reference_rate(cfg, a_host, budget_s=args.cpu_budget)
 
     validator = None
     if dist.world == 1 and args.validate:
         validator = _validator_timing(dev, peaks, peak_kind, lib)
+
+    # N > 1: the multi-GPU schedules of the larger configs, with a parity gate
+    multi = _multi_gpu(args, dist, dev, peaks) if dist.world > 1 and args.multi else None
 
     shapes = None
     if dist.world == 1 and args.shapes:
@@ -363,12 +396,7 @@ def run_ours(args, dist: Dist):
                         if dist.world == 1 and cfg.name in REFERENCE_PUBLISHED_S else None),
         "dtype": "f32", "data": "synthetic",
         "tflops": tflops,
-        "config": {"workload": cfg.name, "batch": b, "n": n, "global_batch": b * dist.world,
-                   "family": cfg.family, "param": cfg.param, "seed": cfg.seed,
-                   "parallelism": f"batch-sharded x{dist.world} (independent matrices, "
-                                  f"no collective)",
-                   "l2": f"round-robin over {len(pool)} distinct resident inputs "
-                         f"({pool_bytes / 2**20:.0f} MiB > 2x L2)"},
+        "config": _config(cfg, dist.world),
         "roofline": roof,
         "e2e": e2e,
         "cpu_baseline": cpu,
@@ -376,15 +404,16 @@ def run_ours(args, dist: Dist):
         "gpu_launches": launches_per_call * args.steps,
         "launches_per_step": launches_per_call,
     }
-    if shapes is not None:
-        line["shapes"] = shapes
-        line["grid"] = _grid_summary(cfg.name, ms_step, shapes)
     if validator is not None:
         line["validator"] = validator
-    if from_root is not None:
-        line["e2e_from_root"] = from_root
+    if multi is not None:
+        line["parity"] = multi.pop("parity")
+        line["multi_gpu"] = multi
+    if shapes is not None:
+        line["grid"] = _grid_summary(cfg.name, ms_step, shapes)
+        line["shapes"] = shapes
     if dist.rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
 
 
 def _kernel_ms_graph(lib, pool, dev, b, n, reps=20):
@@ -557,113 +586,292 @@ def _e2e(args, cfg, pool, lib, dev, dist):
                     "factorisation on one queue, download on another, two buffer slots"}
 
 
+def _cyclic_shard(cfg, lay, dev) -> torch.Tensor:
+    """This rank's columns of A = X X^T / n + shift I (the config's generator, X seeded
+    N(0,1)), built block by block on the GPU with TF32 off."""
+    n = cfg.n
+    g = torch.Generator(device=dev).manual_seed(cfg.seed)
+    x = torch.randn(n, n, generator=g, device=dev)
+    shard = torch.zeros(n, lay.n_local, device=dev)
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for t in lay.owned():
+            c0, w, lc = t * lay.bs, lay.width(t), lay.local_col(t)
+            blk = (x[c0:] @ x[c0:c0 + w].T) / n
+            blk[:w].diagonal().add_(cfg.param)
+            shard[c0:, lc:lc + w] = torch.tril(blk)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+    del x
+    torch.cuda.empty_cache()
+    return shard
+
+
+def _cyclic_measure(args, dist: Dist, cfg, dev, steps: int, warmup: int, e2e: bool):
+    """b1n32768 through the block-cyclic driver: resident shards, a step copies the pristine
+    shard into the work buffer and factors it; CUDA events around `steps` steps, maximum over
+    ranks. With e2e, also the same with each rank's shard uploaded from and downloaded to
+    pinned host memory inside the timed region."""
+    from linalg_kernels_b200.distributed import CyclicLayout, factor_block_cyclic
+
+    n = cfg.n
+    lay = CyclicLayout(n, dist.world, dist.rank, 256)
+    shard = _cyclic_shard(cfg, lay, dev)
+    work = torch.empty_like(shard)
+    pg = dist.pg if dist.world > 1 else None
+
+    def step(_):
+        work.copy_(shard)
+        factor_block_cyclic(work, lay, pg=pg)
+
+    with ClockSampler(dev.index) as clocks:
+        total_ms, _ = _time_steps(step, [None], steps, warmup, dist)
+    out = {"ms_per_step": dist.max(total_ms) / steps, "clocks": clocks.summary(), "lay": lay,
+           "shard_bytes": shard.numel() * 4}
+    if e2e:
+        host_in = shard.cpu().pin_memory()
+        host_out = torch.empty_like(host_in).pin_memory()
+
+        def hstep():
+            work.copy_(host_in, non_blocking=True)
+            factor_block_cyclic(work, lay, pg=pg)
+            host_out.copy_(work, non_blocking=True)
+
+        for _ in range(2):
+            hstep()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            hstep()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        out["e2e_ms_per_step"] = dist.max(e0.elapsed_time(e1)) / steps
+    del work, shard
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_cyclic(args, dist: Dist):
     """One matrix over all ranks, 1-D block-column-cyclic, NCCL panel broadcasts
     (linalg_kernels_b200.distributed). Inputs are resident shards: every rank builds its own
     columns of A = X X^T / n + shift I. A step copies the pristine shard into the work
     buffer and factors it. Strong scaling: one matrix per step whatever the rank count."""
     from linalg_kernels_b200 import _lib, inputs
-    from linalg_kernels_b200.distributed import CyclicLayout, factor_block_cyclic
 
-    lib = _lib.load()
+    _lib.load()
     dev = torch.device("cuda", dist.local)
     torch.cuda.set_device(dev)
-    peaks, peak_kind = _peaks()
     cfg = inputs.GRID[args.config]
     n = cfg.n
-    lay = CyclicLayout(n, dist.world, dist.rank, 256)
-    g = torch.Generator(device=dev).manual_seed(cfg.seed)
-    x = torch.randn(n, n, generator=g, device=dev)
-    shard = torch.zeros(n, lay.n_local, device=dev)
-    old = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False
-    for t in lay.owned():
-        c0, w, lc = t * lay.bs, lay.width(t), lay.local_col(t)
-        blk = (x[c0:] @ x[c0:c0 + w].T) / n
-        blk[:w].diagonal().add_(cfg.param)
-        shard[c0:, lc:lc + w] = torch.tril(blk)
-    torch.backends.cuda.matmul.allow_tf32 = old
-    del x
-    torch.cuda.empty_cache()
-    work = torch.empty_like(shard)
-
-    def step(_):
-        work.copy_(shard)
-        factor_block_cyclic(work, lay, pg=dist.pg if dist.world > 1 else None)
-
-    with ClockSampler(dev.index) as clocks:
-        total_ms, per = _time_steps(step, [None], args.steps, args.warmup, dist)
-    total_ms = dist.max(total_ms)
-    value = args.steps / (total_ms / 1e3)
-    # e2e: pinned host shard in, factor, pinned host shard out
-    host_in = shard.cpu().pin_memory()
-    host_out = torch.empty_like(host_in).pin_memory()
-    for i in range(2):
-        work.copy_(host_in, non_blocking=True)
-        factor_block_cyclic(work, lay, pg=dist.pg if dist.world > 1 else None)
-        host_out.copy_(work, non_blocking=True)
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.steps):
-        work.copy_(host_in, non_blocking=True)
-        factor_block_cyclic(work, lay, pg=dist.pg if dist.world > 1 else None)
-        host_out.copy_(work, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e2e_ms = dist.max(e0.elapsed_time(e1))
-    nbytes = shard.numel() * 4
+    r = _cyclic_measure(args, dist, cfg, dev, args.steps, args.warmup, e2e=True)
+    value = 1e3 / r["ms_per_step"]
+    nbytes = r["shard_bytes"]
     line = {
         "metric": "matrices/s", "value": value, "unit": "matrices/s", "n_gpus": dist.world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
         "higher_is_better": True, "scaling": "strong",
         "vs_baseline": (value / (1 / REFERENCE_PUBLISHED_S[cfg.name]) if dist.world == 1
                         else None),
         "dtype": "f32", "data": "synthetic", "tflops": value * n ** 3 / 3.0 / 1e12,
         "config": {"workload": cfg.name, "batch": 1, "n": n, "family": cfg.family,
-                   "param": cfg.param, "seed": cfg.seed, "block": lay.bs,
+                   "param": cfg.param, "seed": cfg.seed, "block": r["lay"].bs,
                    "parallelism": f"1-D block-column-cyclic over {dist.world} GPUs, NCCL "
                                   f"broadcast of each factored 256-wide panel",
                    "l2": "input 4 GiB > L2"},
         "roofline": None,
-        "e2e": {"value": dist.world and args.steps / (e2e_ms / 1e3), "unit": "matrices/s",
+        "e2e": {"value": 1e3 / r["e2e_ms_per_step"], "unit": "matrices/s",
                 "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
                 "note": "per rank: its resident shard in and out"},
         "cpu_baseline": None,
-        "clocks": clocks.summary(),
+        "clocks": r["clocks"],
         "gpu_launches": None,
     }
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------------------
+# N > 1: the multi-GPU schedules of the larger configs, each gated against one GPU
+# --------------------------------------------------------------------------------------
+def _agree(dist: Dist, ok: bool) -> bool:
+    """Rank 0's verdict, on every rank (the same collective on all of them)."""
+    t = torch.tensor([1.0 if ok else 0.0], dtype=torch.float64, device="cuda")
+    dist.pg.broadcast(t, src=0)
+    return bool(t.item() > 0.5)
+
+
+def _gate(a: torch.Tensor, l: torch.Tensor, l_one: torch.Tensor, cond: torch.Tensor) -> dict:
+    """The north star's gates for a factor l of a (both (b, n, n) on one GPU) against the
+    one-GPU factor l_one: the device checker's gates (relative residual <= 1e-5, scaled
+    inf-norm residual, structure) and max|L - L_one| <= cond(A) n eps_fp32 max|L_one| per
+    matrix (cond: the generator's per-matrix bound)."""
+    from linalg_kernels_b200 import validate
+
+    good, msg = validate.check_implementation(a, l)
+    v = validate.validate(a, l)
+    cond = cond.to(a.device)
+    n = a.shape[-1]
+    diff = (l - l_one).abs().amax(dim=(1, 2)).double()
+    scale = l_one.abs().amax(dim=(1, 2)).double()
+    bound = cond * n * validate.EPS32 * scale
+    within = bool((diff <= bound).all())
+    return {"ok": bool(good and within), "check": msg or "ok",
+            "rel_residual_max": _sig(float(v["rel_residual"].max())),
+            "max_diff_over_bound": _sig(float((diff / bound).max()))}
+
+
+def _cyclic_parity(dist: Dist, dev, n: int = 4096) -> dict:
+    """One n x n covariance matrix factored by the block-cyclic driver over all ranks,
+    gathered to rank 0 and gated against the one-GPU factor of the same matrix."""
+    from linalg_kernels_b200 import inputs
+    from linalg_kernels_b200.cholesky import custom_kernel
+    from linalg_kernels_b200.distributed import (CyclicLayout, factor_block_cyclic,
+                                                 gather_block_cyclic, scatter_block_cyclic)
+
+    a, cond = inputs.covariance(1, n, 0.5, 48000 + n, device=dev)
+    lay = CyclicLayout(n, dist.world, dist.rank, 256)
+    if lay.nblocks % dist.world:
+        raise ValueError("parity case needs whole rounds of blocks")
+    local = scatter_block_cyclic(a[0], lay)
+    factor_block_cyclic(local, lay, pg=dist.pg)
+    parts = [torch.empty_like(local) for _ in range(dist.world)]
+    dist.pg.all_gather(parts, local)
+    res = {"ok": True}
+    if dist.rank == 0:
+        full = gather_block_cyclic(parts, n, dist.world, 256)
+        res = _gate(a, full[None], custom_kernel(a), cond)
+    res["ok"] = _agree(dist, res["ok"])
+    return res
+
+
+def _sharded(dist: Dist, cfg, dev, steps: int, warmup: int) -> dict:
+    """One config's batch over all ranks (strong scaling: the config's batch, split).
+    resident: every rank factors its own slice (no transfer); from_root: the whole batch on
+    rank 0's GPU, slices out and factors back by NCCL point-to-point (factor_batch_sharded),
+    the first run gated against rank 0's one-GPU factor of the same batch."""
+    from linalg_kernels_b200 import inputs
+    from linalg_kernels_b200.cholesky import custom_kernel
+    from linalg_kernels_b200.distributed import batch_slices, factor_batch_sharded
+
+    b, n = cfg.batch, cfg.n
+    a, cond = inputs.config_input(cfg, device=dev) if dist.rank == 0 else (None, None)
+    res: dict = {}
+    l = factor_batch_sharded(a, b, n, dist.pg, root=0)
+    ok = True
+    if dist.rank == 0:
+        g = _gate(a, l, custom_kernel(a), cond)
+        ok = g["ok"]
+        res["gate"] = {k: v for k, v in g.items() if k != "ok"}
+    res["parity"] = _agree(dist, ok)
+    del l
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        return dist.max(e0.elapsed_time(e1)) / steps
+
+    off, cnt = batch_slices(b, dist.world)[dist.rank]
+    mine = inputs.config_input(cfg, device=dev)[0][off:off + cnt].contiguous() \
+        if dist.rank != 0 else a[off:off + cnt]
+    res["resident_ms"] = _sig(timed(lambda: custom_kernel(mine)))
+    res["from_root_ms"] = _sig(timed(lambda: factor_batch_sharded(a, b, n, dist.pg, root=0)))
+    res["one_gpu_published_ms"] = REFERENCE_PUBLISHED_S[cfg.name] * 1e3
+    res["nvlink_bytes_per_step"] = 2.0 * (b - batch_slices(b, dist.world)[0][1]) * n * n * 4
+    del a, mine
+    torch.cuda.empty_cache()
+    return res
+
+
+def _bcast_ms(dist: Dist, dev, nbytes: int, reps: int = 10) -> float:
+    """NCCL broadcast of nbytes from rank 0 (the largest panel of the block-cyclic driver at
+    n = 32768 is 32 MiB): CUDA events around reps broadcasts, maximum over ranks."""
+    buf = torch.empty(nbytes // 4, dtype=torch.float32, device=dev)
+    for _ in range(3):
+        dist.pg.broadcast(buf, src=0)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        dist.pg.broadcast(buf, src=0)
+    e1.record()
+    torch.cuda.synchronize()
+    return dist.max(e0.elapsed_time(e1)) / reps
+
+
+def _multi_gpu(args, dist: Dist, dev, peaks) -> dict:
+    from linalg_kernels_b200 import inputs
+
+    out: dict = {}
+    cp = _cyclic_parity(dist, dev)
+    out["cyclic_parity_b1n4096"] = cp
+    gates = [cp["ok"]]
+    big = inputs.GRID["b1n32768"]
+    r = _cyclic_measure(args, dist, big, dev, steps=max(1, min(args.steps, 5)), warmup=3,
+                        e2e=False)
+    ms = r["ms_per_step"]
+    bc32 = _bcast_ms(dist, dev, 32 << 20)
+    out["cyclic_b1n32768"] = {
+        "ms_per_step": _sig(ms), "tflops": _sig(big.n ** 3 / 3.0 / (ms / 1e3) / 1e12),
+        "reference_one_gpu_ms": REFERENCE_PUBLISHED_S["b1n32768"] * 1e3,
+        "vs_reference_published": _sig(REFERENCE_PUBLISHED_S["b1n32768"] * 1e3 / ms),
+        "panels": r["lay"].nblocks, "bcast_ms_32MiB": _sig(bc32),
+        "bcast_gbs_32MiB": _sig((32 << 20) / (bc32 / 1e3) / 1e9),
+        "bcast_ms_all_panels_serial": _sig(sum(
+            bc32 * (big.n - j * 256) / big.n for j in range(r["lay"].nblocks))),
+        "parallelism": f"1-D block-column-cyclic over {dist.world} GPUs (256-wide blocks), "
+                       f"NCCL broadcast of each factored panel, strong scaling"}
+    for name in ("b640n512", "b60n1024"):
+        sh = _sharded(dist, inputs.GRID[name], dev, steps=10, warmup=3)
+        gates.append(sh.pop("parity"))
+        out[name] = sh
+    out["parity"] = all(gates)
+    return out
+
+
+def _sig(x: float) -> float:
+    return float(f"{x:.4g}")
+
+
 def _other_shapes(args, skip, dev, peaks, peak_kind, lib):
+    """Every other benchmark-grid entry through custom_kernel on resident inputs: one compact
+    row each, [ms per call, the reference's published ms, its ratio to ours, roofline
+    fraction] (the fraction of measured HBM bandwidth at 8 n^2 bytes per matrix for n <= 256,
+    of the TF32 rate at n^3/3 flops per matrix above)."""
     from linalg_kernels_b200 import inputs
     from linalg_kernels_b200.cholesky import custom_kernel
 
-    out = []
+    out = {"cols": ["ms", "ref_ms", "vs_ref", "frac"],
+           "frac": "of measured hbm_gbs (n<=256) / of bf16_tflops/2 (n>256)"}
     names = [k for k in inputs.GRID if k != skip and (args.big or k != "b1n32768")]
     for name in names:
         cfg = inputs.GRID[name]
         pool, pool_bytes = _pool(cfg, dev, 0, max_inputs=16)
         # enough calls that the timed region is ~ms long (the event bracket's fixed cost
         # is then noise): 200 for the microsecond shapes, at most 20 for the others
-        steps = 200 if cfg.n <= 128 else max(3, min(args.steps, 20))
+        steps = 200 if cfg.n <= 128 else max(3, min(args.steps, 20 if cfg.n < 32768 else 5))
         total, per = _time_steps(custom_kernel, pool, steps, 3, _NoDist())
         ms = total / steps
-        value = cfg.batch / (ms / 1e3)
-        row = {"workload": name, "ms_per_step": ms, "matrices_per_s": value,
-               "tflops": value * cfg.n ** 3 / 3.0 / 1e12,
-               "reference_ms": REFERENCE_PUBLISHED_S[name] * 1e3,
-               "vs_reference_published": REFERENCE_PUBLISHED_S[name] * 1e3 / ms}
         if cfg.n <= 256:
-            row["hbm_frac_of_measured"] = 8.0 * cfg.n ** 2 * cfg.batch / (ms / 1e3) / 1e9 / \
-                peaks["hbm_gbs"]
+            frac = 8.0 * cfg.n ** 2 * cfg.batch / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]
         else:
-            row["tf32_frac_of_measured"] = row["tflops"] / (peaks["bf16_tflops"] / 2.0)
-        out.append(row)
+            frac = cfg.batch * cfg.n ** 3 / 3.0 / (ms / 1e3) / 1e12 / (peaks["bf16_tflops"] / 2.0)
+        ref_ms = REFERENCE_PUBLISHED_S[name] * 1e3
+        out[name] = [_sig(ms), _sig(ref_ms), _sig(ref_ms / ms), _sig(frac)]
         del pool
         torch.cuda.empty_cache()
     return out
@@ -717,57 +925,17 @@ def _validator_timing(dev, peaks, peak_kind, lib, names=("b1024n64", "b640n512",
     return rows
 
 
-def _from_root(args, cfg, dev, dist):
-    """Batch sharding end to end from one GPU: the global batch (world x batch matrices of
-    the config) sits on rank 0's GPU; each step, factor_batch_sharded sends every rank its
-    slice by NCCL point-to-point, each rank factors it, and the factors come back to rank 0.
-    The same input every step; CUDA events per rank around K steps, maximum over ranks."""
-    from linalg_kernels_b200 import inputs
-    from linalg_kernels_b200.distributed import factor_batch_sharded
-
-    b, n = cfg.batch, cfg.n
-    total = b * dist.world
-    a = None
-    if dist.rank == 0:
-        c = inputs.Config(cfg.name, total, n, cfg.family, cfg.param, cfg.seed)
-        a, _ = inputs.config_input(c, device=dev)
-
-    def step():
-        factor_batch_sharded(a, total, n, dist.pg, root=0)
-
-    steps = max(3, min(args.steps, 50))
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    ms = dist.max(e0.elapsed_time(e1)) / steps
-    moved = 2.0 * (total - b) * n * n * 4  # slices out and factors back (rank 0's own stays)
-    return {"value": total / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms,
-            "global_batch": total, "steps": steps, "nvlink_bytes_per_step": moved,
-            "path": "input on rank 0's GPU; slices out and factors back by NCCL "
-                    "point-to-point (factor_batch_sharded)"}
-
-
 def _grid_summary(name, ms_step, shapes):
     """The reference leaderboard's ranking figure (AGENTS.md:58-64): the geometric mean of the
     per-call runtimes over the benchmark-grid entries, ours and the reference's published,
-    over the same entries (b1n32768 only with --big)."""
-    ms = {row["workload"]: row["ms_per_step"] for row in shapes}
+    over the same entries."""
+    ms = {k: v[0] for k, v in shapes.items() if k in REFERENCE_PUBLISHED_S}
     ms[name] = ms_step
     names = [k for k in ms if k in REFERENCE_PUBLISHED_S]
     ours = math.exp(sum(math.log(ms[k]) for k in names) / len(names))
     ref = math.exp(sum(math.log(REFERENCE_PUBLISHED_S[k] * 1e3) for k in names) / len(names))
-    return {"entries": len(names), "geomean_ms": ours, "reference_geomean_ms": ref,
-            "vs_reference_published": ref / ours}
+    return {"entries": len(names), "geomean_ms": _sig(ours), "reference_geomean_ms": _sig(ref),
+            "vs_reference_published": _sig(ref / ours)}
 
 
 GEMM_PROBES = {
@@ -860,10 +1028,12 @@ def main(argv=None):
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--shapes", action=argparse.BooleanOptionalAction, default=True,
                     help="also time the other benchmark shapes (N=1 only)")
-    ap.add_argument("--big", action="store_true", help="include b1n32768 in --shapes")
-    ap.add_argument("--from-root", action="store_true",
-                    help="N>1: also time batch sharding end to end from rank 0's GPU "
-                         "(NCCL point-to-point out and back)")
+    ap.add_argument("--big", action=argparse.BooleanOptionalAction, default=True,
+                    help="include b1n32768 in --shapes")
+    ap.add_argument("--multi", action=argparse.BooleanOptionalAction, default=True,
+                    help="N>1: also run the multi-GPU schedules (b1n32768 block-cyclic, batch "
+                         "sharding of b640n512 and b60n1024 from rank 0's GPU) after a parity "
+                         "gate of each against the one-GPU factor")
     ap.add_argument("--validate", action="store_true",
                     help="also time the device-side checker (chol_validate_f32) (N=1 only)")
     ap.add_argument("--cyclic", action="store_true",

@@ -83,8 +83,13 @@ CHOL_API size_t chol_workspace_bytes(int64_t batch, int64_t n);
  *   A, L   : device pointers to batch*n*n floats; A == L allowed (in place), partial overlap rejected
  *   info   : NULL or device pointer to batch ints (written on the queue)
  *   queue  : cudaStream_t as void*
- * The workspace (if the size needs one) is a per-device cache grown with cudaMalloc on
- * first use for a size; call chol_potrf_batched_ws_f32 to supply your own instead.
+ * The workspace (if the size needs one) is ONE cache per device, shared by every queue and
+ * host thread, grown with cudaMalloc (after cudaDeviceSynchronize, since queued work may
+ * still read the old buffer) when a call needs more than it holds. Consequences: calls that
+ * overlap on the GPU (different queues, or host threads without ordering) race on it and
+ * must be serialised by the caller, and a call that grows it cannot be captured into a CUDA
+ * graph. Callers that overlap or capture calls supply a workspace per queue through
+ * chol_potrf_batched_ws_f32 instead.
  */
 CHOL_API int chol_potrf_batched_f32(const float* A, float* L, int64_t batch, int64_t n,
                            int* info, void* queue);
@@ -103,11 +108,12 @@ CHOL_API int chol_potrf_batched_ws_f32(const float* A, float* L, int64_t batch, 
  * always allocates its output and workspaces per call. For callers that cannot call
  * cudaMalloc (a host that owns all device memory through its own pool, or a path where
  * cudaMalloc's implicit device synchronisation is not allowed): the caller passes A, L
- * and info as usual, and the only scratch (the 64 x 64 inverse diagonal blocks of the
- * blocked path, 16 KiB per matrix with n > 64) comes from a fixed 4 MiB device array
- * inside the library, held on every GPU that loads the library until exit. Problems that
- * need more (batch > 256 when n > 128) return CHOL_ERR_SCRATCH_LIMIT; n <= 128 needs none
- * (with the default options).
+ * and info as usual, and the scratch comes from a fixed 4 MiB + 1 KiB device array inside
+ * the library, held on every GPU that loads the library until exit. A call needs 16 KiB per
+ * matrix with n > 128 (the 64 x 64 inverse diagonal blocks of the blocked path) plus its
+ * counters, so at most 256 such matrices per call; larger batches return
+ * CHOL_ERR_SCRATCH_LIMIT. n <= 128 needs none (with the default options). The optional
+ * regions of the blocked schedule are taken from the array when they fit after that.
  * The first call on a device looks up the array's device address with that device
  * current; make that first call before any stream capture. All calls share the array:
  * calls that overlap on the GPU race and must be serialised by the caller.
@@ -148,23 +154,53 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   steps over every row of the panel. */
 #define CHOL_OPT_PANEL_INVERSE 6
 /*   CHOL_OPT_OVERLAP_CALLS: 1 (default) = a call with n <= 64 whose A, L and info are
- *   disjoint from those of the calls still possibly running on the same queue starts
- *   loading before they finish (it still completes after them); 0 = every call waits for
- *   the previous kernel on its queue before reading. */
+ *   disjoint from those of this library's calls still possibly running on the same queue
+ *   starts loading before they finish (it still completes after them). Each CTA first checks
+ *   on the device that the previous call on the queue is still running; if it is not, other
+ *   work may have been enqueued in between (a kernel writing this call's input, say), and
+ *   the CTA waits for everything before it as usual. 0 = every call waits for the previous
+ *   work on its queue before reading. */
 #define CHOL_OPT_OVERLAP_CALLS 7
 /*   CHOL_OPT_MID_KERNEL: 1 (default) = 64 < n <= 128 is factored by one launch with one CTA
  *   per matrix held in shared memory, needing no workspace; 0 = the blocked schedule (the
  *   workspace sizes then follow it: size workspaces after setting this). */
 #define CHOL_OPT_MID_KERNEL 8
+/*   CHOL_OPT_WAIT_LIMIT_US: bound, in microseconds, of the waits in which one CTA waits for
+ *   a tile another CTA publishes (the diagonal-block kernel); 0 = the default, 2 s. A wait
+ *   that runs out records CHOL_ERR_WAIT_TIMEOUT (see chol_status_check) and makes the
+ *   launch's remaining tasks return; the factor of that call is then invalid. The waits on
+ *   the TMA and tensor-core completions of one CTA keep a fixed 2 s bound. */
+#define CHOL_OPT_WAIT_LIMIT_US 9
 CHOL_API int chol_set_option(int option, int value);
+
+/*
+ * Counts, on the current device since the library was loaded, of the CTAs of n <= 64 calls
+ * that started before their predecessor on the queue finished (*started_early), and of those
+ * whose early start the device-side predecessor check withdrew (*withdrawn). Synchronous
+ * (reads device memory); for tests and diagnostics. Either pointer may be NULL.
+ */
+CHOL_API int chol_overlap_stats(int64_t* started_early, int64_t* withdrawn);
 
 /*
  * Synchronises the queue, then reads and clears the device status word that the kernels'
  * bounded waits write on expiry. Returns CHOL_OK, CHOL_ERR_WAIT_TIMEOUT or
- * CHOL_ERR_DEVICE. (The reference's flag waits have no bound and no status,
+ * CHOL_ERR_DEVICE. The word is per device and sticky: CHOL_ERR_WAIT_TIMEOUT means that at
+ * least one call on the device since the last check has an invalid result. It does not
+ * affect later calls (each launch aborts on its own timeouts only). The factor entry points
+ * do not read it, since that needs a synchronisation; callers that need the guarantee check
+ * it after their calls. (The reference's flag waits have no bound and no status,
  * cholesky/cholesky.py:3588-3598, 4846-4853.)
  */
 CHOL_API int chol_status_check(void* queue);
+
+/*
+ * Test hook for the bounded waits: one CTA waits, with the same bounded flag wait the
+ * diagonal-block kernel uses, until words[0] == value (words: 2 device ints, the second the
+ * launch's abort word, normally both 0). A flag that nothing sets makes the wait run out
+ * after CHOL_OPT_WAIT_LIMIT_US, and chol_status_check then reports CHOL_ERR_WAIT_TIMEOUT.
+ * No counterpart in the reference, whose flag waits are unbounded.
+ */
+CHOL_API int chol_test_flag_wait(int* words, int value, void* queue);
 
 /*
  * Host-side helper: copies info (batch ints, device) to the host after synchronising

@@ -33,6 +33,7 @@ CHOL_OPT_CHAIN_SMS = 5
 CHOL_OPT_PANEL_INVERSE = 6
 CHOL_OPT_OVERLAP_CALLS = 7
 CHOL_OPT_MID_KERNEL = 8
+CHOL_OPT_WAIT_LIMIT_US = 9
 ENGINE_AUTO, ENGINE_FMA, ENGINE_TENSOR = 0, 1, 2
 
 _i64 = ctypes.c_int64
@@ -53,6 +54,8 @@ SIGNATURES: dict[str, tuple] = {
     "chol_launch_count": (_i64, [_i64, _i64]),
     "chol_set_option": (_int, [_int, _int]),
     "chol_status_check": (_int, [_vp]),
+    "chol_overlap_stats": (_int, [ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "chol_test_flag_wait": (_int, [_vp, _int, _vp]),
     "chol_info_check": (_int, [_vp, _i64, _vp, ctypes.POINTER(_i64)]),
     "chol_block_potrf_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "chol_gemm_nt_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64,

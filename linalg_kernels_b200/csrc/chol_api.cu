@@ -578,6 +578,9 @@ int prepare_kernels(int /*device*/) {
              : CHOL_ERR_DEVICE;
 }
 
+uint64_t g_wait_limit_ns = 2000000000ull;
+uint64_t wait_limit_ns() { return g_wait_limit_ns; }
+
 int g_gemm_engine = 0;
 // Fused panel step (chol_panel.cu) instead of the three-launch step: 1 always, 0 never,
 // -1 auto. Auto currently means never: measured per step, the fused kernel (one warp factors
@@ -714,12 +717,32 @@ int chol_set_option(int option, int value) {
     g_panel_inverse = value;
     return CHOL_OK;
   }
+  if (option == CHOL_OPT_WAIT_LIMIT_US) {
+    if (value < 0 || value > 60000000) return CHOL_ERR_INVALID_ARG;
+    g_wait_limit_ns = value == 0 ? 2000000000ull : uint64_t(value) * 1000ull;
+    return CHOL_OK;
+  }
   if (option == CHOL_OPT_FUSED_PANEL) {
     if (value < -1 || value > 1) return CHOL_ERR_INVALID_ARG;
     g_fused_panel = value;
     return CHOL_OK;
   }
   return CHOL_ERR_INVALID_ARG;
+}
+
+int chol_overlap_stats(int64_t* started_early, int64_t* withdrawn) {
+  int dev = 0, st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  return overlap_stats(started_early, withdrawn);
+}
+
+int chol_test_flag_wait(int* words, int value, void* queue) {
+  if (words == nullptr || (reinterpret_cast<uintptr_t>(words) & 3)) return CHOL_ERR_INVALID_ARG;
+  int dev = 0, st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  return launch_flag_wait(words, value, static_cast<cudaStream_t>(queue));
 }
 
 int chol_status_check(void* queue) {

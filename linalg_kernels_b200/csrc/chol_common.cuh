@@ -167,6 +167,8 @@ cudaError_t prepare_mid();
 int launch_mid(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q);
 // Overlap of back-to-back independent small calls on one queue (on by default).
 void set_overlap_small(int on);
+// CTAs of small calls that started early / whose early start the device check withdrew.
+int overlap_stats(int64_t* started_early, int64_t* withdrawn);
 int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaStream_t q,
                       bool pdl);
 // Zeros of L right of each row's 64-wide diagonal block (columns >= 64 * (r / 64 + 1)).
@@ -222,6 +224,10 @@ int launch_gemm_tc_prelo(const GemmArgs& g, const float* lo, int64_t ldlo, cudaS
                          bool pdl);
 cudaError_t prepare_tc();
 int read_and_clear_status(int* out);
+// Bound of the inter-CTA flag waits (CHOL_OPT_WAIT_LIMIT_US; 2 s by default).
+uint64_t wait_limit_ns();
+// One CTA waiting with the bounded flag wait for words[0] == value (words[1]: abort word).
+int launch_flag_wait(int* words, int value, cudaStream_t q);
 // Device address of the status word (for kernels in other translation units).
 int* device_status_ptr();
 // Fused 64-wide panel step (chol_panel.cu).

@@ -40,6 +40,8 @@ namespace {
 constexpr int kDT = 256;   // threads: a 16 x 16 grid of 4 x 4 output blocks
 constexpr int kDLD = 68;   // shared tile row stride (floats)
 constexpr int kFlagO = 256, kFlagW = 512;
+// Flag slot 255 of the first matrix (no task uses slots 16..255) is the launch's abort word.
+constexpr int kFlagAbort = 255;
 
 struct DiagArgs {
   float* L;            // (0, 0) of the diagonal block of matrix 0
@@ -53,6 +55,7 @@ struct DiagArgs {
   int64_t batch;
   int nb, want_v, epoch;
   int* status;
+  uint64_t limit_ns;   // bound of every flag wait
 };
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -65,20 +68,26 @@ __device__ __forceinline__ void st_release(int* p, int v) {
 }
 
 // All threads: true once *flag == epoch. Thread 0 polls; false (for every thread) when the
-// time limit passes or another CTA has already recorded an error.
-__device__ __forceinline__ bool cta_wait(const int* flag, int epoch, int* status) {
+// time limit passes or another CTA of the same launch has already given up. A CTA that gives
+// up records CHOL_ERR_WAIT_TIMEOUT in the library's status word (read and cleared by
+// chol_status_check) and writes its launch's epoch into the launch's abort word, so the
+// other waiters of this launch return too. Other launches do not look at either word: an
+// earlier failure does not make later calls drop their work.
+__device__ __forceinline__ bool cta_wait(const int* flag, int epoch, int* status, int* abort,
+                                         uint64_t limit_ns) {
   int ok = 1;
   if (threadIdx.x == 0 && ld_acquire(flag) != epoch) {
     const uint64_t t0 = tcx::global_ns();
     for (;;) {
       __nanosleep(32);
       if (ld_acquire(flag) == epoch) break;
-      if (*reinterpret_cast<volatile int*>(status) != 0) {
+      if (*reinterpret_cast<volatile int*>(abort) == epoch) {
         ok = 0;
         break;
       }
-      if (tcx::global_ns() - t0 > tcx::kWaitLimitNs) {
+      if (tcx::global_ns() - t0 > limit_ns) {
         atomicExch(status, CHOL_ERR_WAIT_TIMEOUT);
+        atomicExch(abort, epoch);
         ok = 0;
         break;
       }
@@ -332,6 +341,7 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   float* Lm = a.L + mi * a.mstride;
   float* Vm = a.V + mi * a.vstride;
   int* F = a.flags + mi * kDiagFlags;
+  int* abort_w = a.flags + kFlagAbort;
   const int ep = a.epoch;
   const int64_t ld = a.ld, ldv = a.ldv;
   auto tileL = [&](int bi, int bj) { return Lm + int64_t(bi) * 64 * ld + bj * 64; };
@@ -368,8 +378,8 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
       inverse_blocked64(Ys, rdiag, Xs, Ws);
     }
     for (int p = 0; p < j; ++p) {
-      if (!cta_wait(&F[kFlagO + i * 16 + p], ep, a.status)) return;
-      if (!cta_wait(&F[kFlagO + j * 16 + p], ep, a.status)) return;
+      if (!cta_wait(&F[kFlagO + i * 16 + p], ep, a.status, abort_w, a.limit_ns)) return;
+      if (!cta_wait(&F[kFlagO + j * 16 + p], ep, a.status, abort_w, a.limit_ns)) return;
       stage_t(Xs, tileL(i, p), ld);
       stage_t(Ys, tileL(j, p), ld);
       __syncthreads();
@@ -389,7 +399,7 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
       }
       put_transposed(Xs, m, tr, tc);
     }
-    if (!cta_wait(&F[j], ep, a.status)) return;
+    if (!cta_wait(&F[j], ep, a.status, abort_w, a.limit_ns)) return;
     stage_t(Ys, tileT(j), ldt);  // Ys[k][c] = T_j[c][k]
     __syncthreads();
     zero(acc);
@@ -411,8 +421,8 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   } else {
     // ---------------- W(i, j) ----------------
     for (int p = j; p < i; ++p) {
-      if (!cta_wait(&F[kFlagO + i * 16 + p], ep, a.status)) return;
-      if (!cta_wait(p == j ? &F[j] : &F[kFlagW + p * 16 + j], ep, a.status)) return;
+      if (!cta_wait(&F[kFlagO + i * 16 + p], ep, a.status, abort_w, a.limit_ns)) return;
+      if (!cta_wait(p == j ? &F[j] : &F[kFlagW + p * 16 + j], ep, a.status, abort_w, a.limit_ns)) return;
       stage_t(Xs, tileL(i, p), ld);
       stage_n(Ys, tileV(p, j), ldv);
       __syncthreads();
@@ -424,7 +434,7 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
     for (int u = 0; u < 4; ++u)
       *reinterpret_cast<float4*>(Ys + (4 * tr + u) * kDLD + 4 * tc) =
           make_float4(acc[u][0].x, acc[u][0].y, acc[u][1].x, acc[u][1].y);
-    if (!cta_wait(&F[i], ep, a.status)) return;
+    if (!cta_wait(&F[i], ep, a.status, abort_w, a.limit_ns)) return;
     stage_t(Xs, tileV(i, i), ldv);
     __syncthreads();
     zero(acc);
@@ -461,7 +471,21 @@ __global__ void __launch_bounds__(kDT, 1) diag_block_kernel(DiagArgs a) {
   publish(&F[d], ep);
 }
 
+// One CTA waits with cta_wait for words[0] == value; words[1] is its abort word. For the
+// test of the wait bound (chol_test_flag_wait): a flag that nothing sets.
+__global__ void __launch_bounds__(64) flag_wait_kernel(int* words, int value, int* status,
+                                                       uint64_t limit_ns) {
+  cta_wait(words, value, status, words + 1, limit_ns);
+}
+
 }  // namespace
+
+int launch_flag_wait(int* words, int value, cudaStream_t q) {
+  int* status = device_status_ptr();
+  if (status == nullptr) return CHOL_ERR_DEVICE;
+  return status_from(launch_pdl(flag_wait_kernel, dim3(1), dim3(64), 0, q, false, words, value,
+                                status, wait_limit_ns()));
+}
 
 int launch_diag_block(float* L11, int64_t mstride, int64_t ld, float* V, int64_t vstride,
                       int64_t ldv, int nb, bool want_v, int* flags, unsigned* ticket, int epoch,
@@ -488,6 +512,7 @@ int launch_diag_block(float* L11, int64_t mstride, int64_t ld, float* V, int64_t
   a.epoch = epoch;
   a.status = device_status_ptr();
   if (a.status == nullptr) return CHOL_ERR_DEVICE;
+  a.limit_ns = wait_limit_ns();
   const int64_t ntask = 1 + int64_t(nb) * (nb - 1) / 2 + (want_v ? int64_t(nb) * (nb - 1) / 2 : 0);
   const int64_t ctas = ntask * batch;
   if (ctas > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;

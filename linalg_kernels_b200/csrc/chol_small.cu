@@ -84,6 +84,21 @@ __device__ __forceinline__ int quad_off(int r, int c) {
   return t * 1024 + rr * 32 + ((((cc >> 2) ^ (rr & 7))) << 2) + (cc & 3);
 }
 
+// Per-queue CTA counters of the overlap check: for run-table entry e and call parity p,
+// g_run_ctas[e][p][0] counts the CTAs of that queue's small calls of parity p that have
+// started, [1] those that have finished (both wrap modulo 2^32; only their difference is
+// used). g_overlap_stats[0] counts CTAs that started early, [1] CTAs whose early start the
+// check withdrew.
+constexpr int kRunEntries = 64;
+__device__ unsigned g_run_ctas[kRunEntries][2][2];
+__device__ unsigned long long g_overlap_stats[2];
+
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // FULL: n == NP and 16-byte aligned rows (vector path). Otherwise scalar loads with
 // identity padding of rows/columns n..NP-1.
 //
@@ -95,11 +110,26 @@ __device__ __forceinline__ int quad_off(int r, int c) {
 //      of back-to-back calls whose output tensors reuse one allocation);
 //   2  at the end (all buffers disjoint).
 // With 1 or 2 a call's loads and pivot chain run under the previous call's factor and stores.
+//
+// The host only knows the library's own calls. Work that someone else enqueued on the queue
+// between two calls (a kernel that writes this call's input, e.g. the clone in
+// custom_kernel(clone(data))) is invisible to it, and a kernel that reads before
+// griddepcontrol.wait has no guarantee of seeing that work's writes. So each CTA checks on
+// the device that its predecessor is the library's previous call on this queue, still
+// running: prev_ctr counts the started and finished CTAs of that call and of the earlier
+// calls of the same parity on the queue. Started != finished means one of them is still
+// running, so this grid began before the previous call completed. Anything enqueued
+// between the two (a kernel, copy or memset without programmatic serialisation) would have
+// had to wait for that completion, and this grid for it, so nothing was. Calls on one queue
+// complete in order (each takes griddepcontrol.wait), and the next call of the same parity
+// cannot start before every CTA of this grid has passed this check, so only calls up to the
+// predecessor contribute. Started == finished proves nothing: the CTA then takes the wait
+// at its start. my_ctr is this call's pair (nullptr: no counting, early must be 0).
 template <int NP, bool FULL>
 __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
     small_potrf_kernel(const float* __restrict__ A, float* __restrict__ L, int64_t batch, int n,
                        int* __restrict__ info, const __grid_constant__ CUtensorMap out_map,
-                       int early) {
+                       int early, const unsigned* prev_ctr, unsigned* my_ctr) {
   constexpr int LPM = SmallShape<NP>::LPM;
   constexpr int R = SmallShape<NP>::R;
   constexpr int MPW = SmallShape<NP>::MPW;
@@ -129,6 +159,27 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
   const int64_t mbase = (int64_t(blockIdx.x) * small_warps<NP>() + warp) * MPW;
   if (FULL) n = NP;
 
+  if (my_ctr != nullptr) {
+    __shared__ int s_early;
+    if (threadIdx.x == 0) {
+      int e = early;
+      if (e > 0) {
+        // finished first, then started: a difference means some CTA ran after this one began
+        const unsigned fin = ld_relaxed_u32(prev_ctr + 1);
+        const unsigned sta = ld_relaxed_u32(prev_ctr + 0);
+        if (sta == fin) {
+          e = 0;
+          atomicAdd(&g_overlap_stats[1], 1ull);
+        } else {
+          atomicAdd(&g_overlap_stats[0], 1ull);
+        }
+      }
+      atomicAdd(my_ctr, 1u);
+      s_early = e;
+    }
+    __syncthreads();
+    early = s_early;
+  }
   if (early == 0) griddep_wait();
   griddep_launch();
 
@@ -295,6 +346,10 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
     if (m < batch) info[m] = (fail > n) ? 0 : fail;
   }
   if (early == 2) griddep_wait();
+  if (my_ctr != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(my_ctr + 1, 1u);
+  }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_small_enc = nullptr;
@@ -360,7 +415,11 @@ bool cached_out_map(CUtensorMap* out, float* L, int64_t batch, int n, int np) {
 // ---- overlap of back-to-back small calls ----
 // Per (device, queue), the calls that may still be running: a call that took its dependency
 // wait at the start ended the run (everything before it had completed); a call that waits
-// later joins it. Any other kernel launched on the queue clears the run.
+// later joins it. Any other kernel the library launches on the queue clears the run; work
+// enqueued by others is caught on the device (small_potrf_kernel's predecessor check).
+// Entries are bound to their (device, queue) for the life of the process, so the device
+// counters of an entry only ever count that queue's CTAs; queues beyond the first
+// kRunEntries get no entry and their calls never start early.
 struct Span {
   uintptr_t lo = 0, hi = 0;
   bool meets(const Span& o) const { return lo < o.hi && o.lo < hi; }
@@ -371,14 +430,16 @@ struct SmallCall {
 struct QueueRun {
   cudaStream_t q = nullptr;
   int dev = -1;  // the same handle (the legacy default queue) exists on every device
+  bool used = false;
   int count = 0;
+  unsigned parity = 0;  // parity of the next call on this queue
   SmallCall calls[8];
 };
 int g_overlap_small = 1;
 std::mutex g_run_mu;
-QueueRun g_runs[16];
-int g_run_next = 0;
+QueueRun g_runs[kRunEntries];
 thread_local bool t_in_small_launch = false;
+unsigned* g_run_ctas_dev[64] = {};  // device address of g_run_ctas, per device
 
 int current_device() {
   int d = -1;
@@ -386,9 +447,20 @@ int current_device() {
   return d;
 }
 
+// The entry of (q, dev), bound on first use; nullptr when the table is full.
 QueueRun* find_run(cudaStream_t q, int dev) {
   for (auto& r : g_runs)
-    if (r.count > 0 && r.q == q && r.dev == dev) return &r;
+    if (r.used && r.q == q && r.dev == dev) return &r;
+  for (auto& r : g_runs) {
+    if (!r.used) {
+      r.used = true;
+      r.q = q;
+      r.dev = dev;
+      r.count = 0;
+      r.parity = 0;
+      return &r;
+    }
+  }
   return nullptr;
 }
 
@@ -432,33 +504,37 @@ int launch_np(const float* A, float* L, int64_t batch, int n, int* info, cudaStr
                  reinterpret_cast<uintptr_t>(info) + uintptr_t(batch) * sizeof(int)};
   const int dev = current_device();
   std::lock_guard<std::mutex> lock(g_run_mu);
-  QueueRun* run = find_run(q, dev);
+  unsigned* ctrs = (dev >= 0 && dev < 64) ? g_run_ctas_dev[dev] : nullptr;
+  QueueRun* run = ctrs != nullptr ? find_run(q, dev) : nullptr;
   const int early = may_start_early(run, call);
+  const unsigned* prev_ctr = nullptr;
+  unsigned* my_ctr = nullptr;
+  if (run != nullptr) {
+    const int entry = int(run - g_runs);
+    my_ctr = ctrs + (entry * 2 + int(run->parity)) * 2;
+    prev_ctr = ctrs + (entry * 2 + int(run->parity ^ 1u)) * 2;
+  }
   t_in_small_launch = true;
   if (full)
     e = launch_pdl(small_potrf_kernel<NP, true>, dim3(unsigned(blocks)), dim3(small_warps<NP>() * 32),
-                   smem, q, true, A, L, batch, n, info, map, early);
+                   smem, q, true, A, L, batch, n, info, map, early, prev_ctr, my_ctr);
   else
     e = launch_pdl(small_potrf_kernel<NP, false>, dim3(unsigned(blocks)),
-                   dim3(small_warps<NP>() * 32), smem, q, true, A, L, batch, n, info, map, early);
+                   dim3(small_warps<NP>() * 32), smem, q, true, A, L, batch, n, info, map, early,
+                   prev_ctr, my_ctr);
   t_in_small_launch = false;
   if (e != cudaSuccess) {
     if (run != nullptr) run->count = 0;
     return status_from(e);
   }
+  if (run == nullptr) return CHOL_OK;
+  run->parity ^= 1u;
   if (early > 0) {
     run->calls[run->count++] = call;  // may_start_early needs a run with room
   } else {
     // this call waits for everything before it: the run restarts with it
-    QueueRun* r = run;
-    if (r == nullptr) {
-      r = &g_runs[g_run_next];
-      g_run_next = (g_run_next + 1) % int(sizeof(g_runs) / sizeof(g_runs[0]));
-    }
-    r->q = q;
-    r->dev = dev;
-    r->count = 0;
-    r->calls[r->count++] = call;
+    run->count = 0;
+    run->calls[run->count++] = call;
   }
   return CHOL_OK;
 }
@@ -476,8 +552,18 @@ cudaError_t set_smem_np() {
 
 }  // namespace
 
+// Per device (current at the call): kernel attributes and the device address of the
+// overlap counters (host code cannot pass the symbol itself to a kernel).
 cudaError_t prepare_small() {
   cudaError_t e;
+  int dev = -1;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64) {
+    void* p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, g_run_ctas)) != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(g_run_mu);
+    g_run_ctas_dev[dev] = static_cast<unsigned*>(p);
+  }
   if ((e = set_smem_np<4>()) != cudaSuccess) return e;
   if ((e = set_smem_np<8>()) != cudaSuccess) return e;
   if ((e = set_smem_np<16>()) != cudaSuccess) return e;
@@ -499,6 +585,16 @@ void set_overlap_small(int on) {
   std::lock_guard<std::mutex> lock(g_run_mu);
   g_overlap_small = on;
   for (auto& r : g_runs) r.count = 0;
+}
+
+// CTAs that started early / whose early start the device check withdrew, on the current
+// device since the library was loaded (reads device memory: synchronous).
+int overlap_stats(int64_t* started_early, int64_t* withdrawn) {
+  unsigned long long v[2] = {0, 0};
+  if (cudaMemcpyFromSymbol(v, g_overlap_stats, sizeof(v)) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if (started_early) *started_early = int64_t(v[0]);
+  if (withdrawn) *withdrawn = int64_t(v[1]);
+  return CHOL_OK;
 }
 
 int launch_small(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q) {

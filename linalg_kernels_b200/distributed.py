@@ -6,8 +6,9 @@ cholesky/cholesky.py:5692-5802). Here one process per GPU holds the column block
 row-major in a local ``(n, n_local)`` tensor. For every block column ``j``:
 
 1. its owner factors the panel ``L[j*bs:, j*bs:(j+1)*bs]`` in place with one
-   ``chol_panel_potrf_f32`` call (64-wide left-looking steps: diagonal factor + inverse,
-   panel solve ``X <- X T^T``, on tensor cores);
+   ``chol_panel_potrf_f32`` call (one diagonal-block launch that factors the ``bs x bs`` top
+   block and writes its inverse ``V``, then one tensor-core GEMM ``X = A21 V^T`` that solves
+   every row below);
 2. the factored panel (rows ``j*bs .. n``, ``bs`` columns, at most 32 MiB at n = 32768) is
    packed contiguously and broadcast by NCCL from the owner into every rank's receive
    buffer (local memory; no kernel reads another GPU's memory);

@@ -9,7 +9,7 @@ LAPACK SPOTRF from the MKL bundled with torch. The outputs L (and info from
 ``torch.linalg.cholesky_ex``) are stored next to the inputs.
 
 Run in the build container (the reference tree is not present on GPU boxes):
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 """
 
 from __future__ import annotations
@@ -89,7 +89,9 @@ def not_spd_cases():
 
 
 def main(argv):
-    root = Path(argv[1]) if len(argv) > 1 else Path("/root/reference")
+    if len(argv) < 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path to the reference tree>")
+    root = Path(argv[1])
     ref = load_reference(root)
     store: dict[str, np.ndarray] = {}
     names = []

@@ -25,14 +25,15 @@ def test_grid_holds_the_configs_and_the_published_times():
 
 
 def test_grid_summary_is_the_geometric_mean():
-    shapes = [{"workload": "b4096n32", "ms_per_step": 0.01},
-              {"workload": "b1n16384", "ms_per_step": 10.0}]
+    # the compact shape rows: [ms per call, published ms, ratio, roofline fraction]
+    shapes = {"cols": ["ms", "ref_ms", "vs_ref", "frac"], "frac": "note",
+              "b4096n32": [0.01, 0.0157, 1.57, 0.5], "b1n16384": [10.0, 15.1, 1.51, 0.2]}
     g = bench._grid_summary("b1024n64", 0.02, shapes)
     assert g["entries"] == 3
-    assert g["geomean_ms"] == pytest.approx((0.01 * 10.0 * 0.02) ** (1 / 3))
+    assert g["geomean_ms"] == pytest.approx((0.01 * 10.0 * 0.02) ** (1 / 3), rel=1e-3)
     ref = (15.7e-3 * 15.1 * 24.1e-3) ** (1 / 3)
-    assert g["reference_geomean_ms"] == pytest.approx(ref)
-    assert g["vs_reference_published"] == pytest.approx(ref / g["geomean_ms"])
+    assert g["reference_geomean_ms"] == pytest.approx(ref, rel=1e-3)
+    assert g["vs_reference_published"] == pytest.approx(ref / g["geomean_ms"], rel=1e-3)
 
 
 def test_test_shapes_table():

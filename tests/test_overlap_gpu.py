@@ -151,3 +151,106 @@ def test_not_spd_info_with_overlap():
             assert int(info[5]) > 0 and int(info.count_nonzero()) == 1
         else:
             assert int(info.count_nonzero()) == 0
+
+
+# ---- work that is not the library's, enqueued on the same queue between two calls ----
+def _stats():
+    lib = _lib.load()
+    early, withdrawn = ctypes.c_int64(), ctypes.c_int64()
+    assert lib.chol_overlap_stats(ctypes.byref(early), ctypes.byref(withdrawn)) == _lib.CHOL_OK
+    return early.value, withdrawn.value
+
+
+@pytest.mark.parametrize("n,batch", [(64, 1024), (32, 4096)])
+def test_evaluator_clone_between_calls(n, batch):
+    # the reference's evaluator calls custom_kernel(clone(data)): a torch kernel writes the
+    # next call's input immediately before the call
+    pool = _pool(n, batch, 5, 700 + n)
+
+    def run(sync=False):
+        outs = []
+        for i in range(25):
+            outs.append(custom_kernel(pool[i % len(pool)].clone()))
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return outs
+
+    got = run()
+    want = _one_at_a_time(run)
+    for g_, w in zip(got, want):
+        assert torch.equal(g_, w)
+
+
+def test_foreign_writes_of_next_input_and_output():
+    # torch kernels write the next call's input (copy_, mul_) and fill the next call's
+    # output buffer, each right before the call
+    n, batch = 64, 1024
+    src = _pool(n, batch, 4, 800)
+    lib = _lib.load()
+    q = ctypes.c_void_p(_lib.current_queue(torch.device(DEV)))
+
+    def run(sync=False):
+        ins = [torch.empty_like(src[0]) for _ in range(4)]
+        outs = [torch.empty_like(src[0]) for _ in range(4)]
+        res = []
+        for i in range(16):
+            k = i % 4
+            ins[k].copy_(src[(i + 1) % 4])
+            if i % 3 == 0:
+                ins[k].mul_(1.5)
+            outs[k].fill_(float("nan"))
+            assert lib.chol_potrf_batched_f32(ctypes.c_void_p(ins[k].data_ptr()),
+                                              ctypes.c_void_p(outs[k].data_ptr()), batch, n,
+                                              None, q) == 0
+            res.append(outs[k].double().sum(dim=(1, 2)))
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return res + outs
+
+    got = run()
+    want = _one_at_a_time(run)
+    for g_, w in zip(got, want):
+        assert torch.equal(g_, w)
+
+
+def test_device_check_withdraws_early_start_after_foreign_kernel():
+    # two calls on disjoint buffers (the host lets the second start early); a torch kernel
+    # between them writes the second call's input. The second call's grid cannot start before
+    # that kernel has completed, and so before the first call has; every one of its CTAs must
+    # see that on the device and take the full wait
+    n, batch = 64, 1024
+    a1, a2, s2 = _pool(n, batch, 3, 900)
+    o1, o2 = torch.empty_like(a1), torch.empty_like(a1)
+    lib = _lib.load()
+    q = ctypes.c_void_p(_lib.current_queue(torch.device(DEV)))
+    ctas = (batch + 3) // 4  # 4 matrices per CTA at n = 64
+    # start a fresh run on the queue: the first call below then waits as usual
+    lib.chol_set_option(_lib.CHOL_OPT_OVERLAP_CALLS, 0)
+    lib.chol_set_option(_lib.CHOL_OPT_OVERLAP_CALLS, 1)
+    torch.cuda.synchronize()
+    e0, w0 = _stats()
+    assert lib.chol_potrf_batched_f32(ctypes.c_void_p(a1.data_ptr()),
+                                      ctypes.c_void_p(o1.data_ptr()), batch, n, None, q) == 0
+    a2.copy_(s2)
+    assert lib.chol_potrf_batched_f32(ctypes.c_void_p(a2.data_ptr()),
+                                      ctypes.c_void_p(o2.data_ptr()), batch, n, None, q) == 0
+    torch.cuda.synchronize()
+    e1, w1 = _stats()
+    assert e1 - e0 == 0
+    assert w1 - w0 == ctas
+    assert torch.equal(o2, custom_kernel(s2))
+
+
+def test_back_to_back_calls_still_start_early():
+    # without foreign work between them, consecutive calls keep overlapping
+    n, batch = 64, 1024
+    pool = _pool(n, batch, 4, 950)
+    torch.cuda.synchronize()
+    e0, _ = _stats()
+    for i in range(40):
+        custom_kernel(pool[i % 4])
+    torch.cuda.synchronize()
+    e1, _ = _stats()
+    assert e1 > e0

@@ -35,7 +35,7 @@ def _factor(entry, a, info):
     return st, out
 
 
-@pytest.mark.parametrize("batch,n", [(96, 32), (7, 200), (16, 512), (256, 130)])
+@pytest.mark.parametrize("batch,n", [(96, 32), (7, 200), (16, 512), (256, 130), (1, 2048)])
 def test_no_alloc_matches_allocating_entry_point(batch, n):
     for call in range(2):
         a, cond = inputs.spectral(batch, n, 100.0, 500 + 17 * n + call)
@@ -53,7 +53,7 @@ def test_no_alloc_matches_allocating_entry_point(batch, n):
 
 def test_no_alloc_rejects_sizes_beyond_its_scratch():
     lib = _lib.load()
-    batch, n = 300, 130  # 300 inverse blocks of 16 KiB + counters > the fixed scratch
+    batch, n = 257, 130  # 257 inverse blocks of 16 KiB + counters > the fixed scratch
     a = torch.eye(n, device=DEV).expand(batch, n, n).contiguous()
     out = torch.empty_like(a)
     st = lib.chol_potrf_batched_noalloc_f32(ctypes.c_void_p(a.data_ptr()),

@@ -251,6 +251,14 @@ CHOL_API int chol_gemm_nt_f32(float* C, int64_t batch, int64_t cstride, int64_t 
 CHOL_API int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv,
                                   int* info, void* queue);
 
+/* chol_panel_potrf_f32 (the one-launch form: w a multiple of 64, <= 1024, 16-byte aligned
+   rows) that also writes the factored panel to out: m x w floats, row-major, contiguous,
+   disjoint from L. The panel solve writes its rows straight into out, so the multi-GPU
+   driver sends out without packing the panel first. CHOL_ERR_UNSUPPORTED for shapes the
+   one-launch form does not take. */
+CHOL_API int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w, float* out,
+                                      int* info, void* queue);
+
 /* chol_gemm_nt_f32 for one matrix whose columns are stored block-cyclically: local column c
    of C (and row c of Q) stands for global column c + (c / col_block) * (col_stride -
    col_block), and lower_only compares that global column with the row. One launch updates

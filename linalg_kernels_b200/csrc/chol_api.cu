@@ -525,8 +525,10 @@ void* panel_scratch(int dev, size_t need) {
 // Panel of width w (w % 64 == 0, w <= 1024): diag_block_kernel factors the w x w top block
 // and writes V = inv(L11); one GEMM solves every row below, X = A21 V^T, into scratch;
 // tf32_lo_kernel copies X back into L (its low-part output stays in scratch, unused).
+// With out != nullptr the solve writes X straight into rows w.. of out (m x w, row-major,
+// contiguous), and the top block is copied there too: the packed panel, ready to send.
 int panel_potrf_inverse(float* L, int64_t ld, int64_t m, int64_t w, int* info, int dev,
-                        cudaStream_t q) {
+                        cudaStream_t q, float* out = nullptr) {
   const int nb = int(w / kBlock);
   const size_t vbytes = size_t(w) * size_t(w) * sizeof(float);
   const size_t fbytes = kDiagFlags * sizeof(int) + 256;
@@ -536,10 +538,17 @@ int panel_potrf_inverse(float* L, int64_t ld, int64_t m, int64_t w, int* info, i
   float* V = reinterpret_cast<float*>(base);
   int* flags = reinterpret_cast<int*>(base + vbytes);
   unsigned* ticket = reinterpret_cast<unsigned*>(flags + kDiagFlags);
-  float* X = reinterpret_cast<float*>(base + vbytes + fbytes);
+  float* scratch_x = reinterpret_cast<float*>(base + vbytes + fbytes);
+  float* X = out != nullptr ? out + w * w : scratch_x;
   if (cudaMemsetAsync(V, 0, vbytes + fbytes, q) != cudaSuccess) return CHOL_ERR_LAUNCH;
   int st = launch_diag_block(L, 0, ld, V, 0, w, nb, m > w, flags, ticket, 1, info, 0, 1, q);
-  if (st || m == w) return st;
+  if (st) return st;
+  if (out != nullptr &&
+      cudaMemcpy2DAsync(out, size_t(w) * sizeof(float), L, size_t(ld) * sizeof(float),
+                        size_t(w) * sizeof(float), size_t(w), cudaMemcpyDeviceToDevice,
+                        q) != cudaSuccess)
+    return CHOL_ERR_LAUNCH;
+  if (m == w) return CHOL_OK;
   GemmArgs x{};
   x.C = X;
   x.ldc = w;
@@ -554,7 +563,7 @@ int panel_potrf_inverse(float* L, int64_t ld, int64_t m, int64_t w, int* info, i
   x.beta = 0.f;
   x.batch = 1;
   if ((st = launch_gemm(x, q, true))) return st;
-  return launch_tf32_lo(X, w, X, w, m - w, w, 1, 0, 0, q, L + w * ld, ld, 0);
+  return launch_tf32_lo(X, w, scratch_x, w, m - w, w, 1, 0, 0, q, L + w * ld, ld, 0);
 }
 
 }  // namespace
@@ -867,6 +876,23 @@ int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv
     if ((st = launch_gemm(x, q, true))) return st;
   }
   return CHOL_OK;
+}
+
+int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w, float* out, int* info,
+                             void* queue) {
+  if (L == nullptr || out == nullptr || m < 0 || w < 0 || w > m || ld < w)
+    return CHOL_ERR_INVALID_ARG;
+  if (m == 0 || w == 0) return CHOL_OK;
+  if (w % kBlock || w > 16 * kBlock || ld % 4 || (reinterpret_cast<uintptr_t>(L) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15) || g_gemm_engine == 1)
+    return CHOL_ERR_UNSUPPORTED;
+  const uintptr_t lo = reinterpret_cast<uintptr_t>(out), hi = lo + uintptr_t(m * w) * 4;
+  const uintptr_t l0 = reinterpret_cast<uintptr_t>(L);
+  if (lo < l0 + uintptr_t((m - 1) * ld + w) * 4 && l0 < hi) return CHOL_ERR_INVALID_ARG;
+  int dev = 0, st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  return panel_potrf_inverse(L, ld, m, w, info, dev, static_cast<cudaStream_t>(queue), out);
 }
 
 int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t ncols, int64_t K,

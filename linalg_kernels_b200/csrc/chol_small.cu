@@ -84,18 +84,22 @@ __device__ __forceinline__ int quad_off(int r, int c) {
   return t * 1024 + rr * 32 + ((((cc >> 2) ^ (rr & 7))) << 2) + (cc & 3);
 }
 
-// Per-queue CTA counters of the overlap check: for run-table entry e and call parity p,
-// g_run_ctas[e][p][0] counts the CTAs of that queue's small calls of parity p that have
-// started, [1] those that have finished (both wrap modulo 2^32; only their difference is
-// used). g_overlap_stats[0] counts CTAs that started early, [1] CTAs whose early start the
+// Per-queue CTA counters of the overlap check: for run-table entry e, call parity p and
+// stripe s, g_run_ctas[e][p][s][0] counts the CTAs (blockIdx.x % kStripes == s) of that
+// queue's small calls of parity p that have started, [1] those that have finished (both wrap
+// modulo 2^32; only their difference is used). The stripes spread the atomics of a grid's
+// CTAs over 32 addresses: on one address they serialise in L2 and delay every CTA's exit.
+// g_overlap_stats[s][0] counts CTAs that started early, [s][1] CTAs whose early start the
 // check withdrew.
 constexpr int kRunEntries = 64;
-__device__ unsigned g_run_ctas[kRunEntries][2][2];
-__device__ unsigned long long g_overlap_stats[2];
+constexpr int kStripes = 32;
+__device__ __align__(16) unsigned g_run_ctas[kRunEntries][2][kStripes][2];
+__device__ unsigned long long g_overlap_stats[kStripes][2];
 
-__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// One 8-byte-aligned load of a {started, finished} counter pair (started in the low word).
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -123,8 +127,10 @@ __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
 // had to wait for that completion, and this grid for it, so nothing was. Calls on one queue
 // complete in order (each takes griddepcontrol.wait), and the next call of the same parity
 // cannot start before every CTA of this grid has passed this check, so only calls up to the
-// predecessor contribute. Started == finished proves nothing: the CTA then takes the wait
-// at its start. my_ctr is this call's pair (nullptr: no counting, early must be 0).
+// predecessor contribute. Started == finished proves nothing: the CTA then takes the full
+// wait and loads its input again (the first loads are issued while the counters are read,
+// so the check adds no latency when it passes). my_ctr is this call's pair (nullptr: no
+// counting, early must be 0).
 template <int NP, bool FULL>
 __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
     small_potrf_kernel(const float* __restrict__ A, float* __restrict__ L, int64_t batch, int n,
@@ -159,31 +165,28 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
   const int64_t mbase = (int64_t(blockIdx.x) * small_warps<NP>() + warp) * MPW;
   if (FULL) n = NP;
 
-  if (my_ctr != nullptr) {
-    __shared__ int s_early;
-    if (threadIdx.x == 0) {
-      int e = early;
-      if (e > 0) {
-        // finished first, then started: a difference means some CTA ran after this one began
-        const unsigned fin = ld_relaxed_u32(prev_ctr + 1);
-        const unsigned sta = ld_relaxed_u32(prev_ctr + 0);
-        if (sta == fin) {
-          e = 0;
-          atomicAdd(&g_overlap_stats[1], 1ull);
-        } else {
-          atomicAdd(&g_overlap_stats[0], 1ull);
-        }
-      }
-      atomicAdd(my_ctr, 1u);
-      s_early = e;
-    }
-    __syncthreads();
-    early = s_early;
+  // ---- overlap check, part 1: the predecessor's CTA counts, one 64-bit snapshot of each
+  // stripe (warp 0, lane s reads stripe s). No static shared memory here: the dynamic buffer
+  // is 1024-byte aligned, so even one static word costs 1 KiB per CTA, and at n = 64 that
+  // is one CTA fewer per SM ----
+  const int stripe = int(blockIdx.x % kStripes);
+  unsigned long long pair = 0;
+  if (my_ctr != nullptr && warp == 0) {
+    if (early > 0) pair = ld_relaxed_u64(prev_ctr + 2 * lane);
+    if (lane == 0) atomicAdd(my_ctr + 2 * stripe, 1u);  // this CTA has started
   }
-  if (early == 0) griddep_wait();
-  griddep_launch();
+  if (early == 0) {
+    griddep_wait();
+    griddep_launch();
+  }
 
-  // ---- load: lower triangle, coalesced, into this warp's staging tiles ----
+  // ---- load: lower triangle, coalesced, into this warp's staging tiles. With early > 0 the
+  // loads are issued while the check's snapshot is in flight, and issued again after the
+  // full wait if the check withdraws the early start ----
+  // pass 0: the loads (speculative when early > 0); pass 1 only when the check withdrew the
+  // early start (one copy of the load code either way)
+#pragma unroll 1
+  for (int pass = 0; pass < 2; ++pass) {
 #pragma unroll 1
   for (int mm = 0; mm < MPW; ++mm) {
     const int64_t m = mbase + mm;
@@ -221,6 +224,21 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
         st[r * LDS + c] = (r == c) ? 1.f : 0.f;
       }
     }
+  }
+  if (pass > 0 || early == 0) break;
+  // ---- overlap check, part 2 (see above): started != finished proves the predecessor
+  // was still running after this grid began. The dependents' trigger comes after the
+  // decision, so no CTA of the next call can have touched the snapshot's counters ----
+  const bool running =
+      __syncthreads_or(warp == 0 && unsigned(pair) != unsigned(pair >> 32)) != 0;
+  if (threadIdx.x == 0) atomicAdd(&g_overlap_stats[stripe][running ? 0 : 1], 1ull);
+  griddep_launch();
+  if (running) break;
+  // withdrawn: the speculative loads may predate writes of work queued before this call
+  cp_async_wait_all();
+  __syncwarp();
+  griddep_wait();
+  early = 0;
   }
   cp_async_wait_all();
   __syncwarp();
@@ -346,10 +364,9 @@ __global__ void __launch_bounds__(small_warps<NP>() * 32, small_min_ctas<NP>())
     if (m < batch) info[m] = (fail > n) ? 0 : fail;
   }
   if (early == 2) griddep_wait();
-  if (my_ctr != nullptr) {
-    __syncthreads();
-    if (threadIdx.x == 0) atomicAdd(my_ctr + 1, 1u);
-  }
+  // finished: counted when warp 0 is done (without waiting for the other warps, which can
+  // only make a later check see this CTA as done early, the safe direction)
+  if (my_ctr != nullptr && threadIdx.x == 0) atomicAdd(my_ctr + 2 * stripe + 1, 1u);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_small_enc = nullptr;
@@ -511,8 +528,8 @@ int launch_np(const float* A, float* L, int64_t batch, int n, int* info, cudaStr
   unsigned* my_ctr = nullptr;
   if (run != nullptr) {
     const int entry = int(run - g_runs);
-    my_ctr = ctrs + (entry * 2 + int(run->parity)) * 2;
-    prev_ctr = ctrs + (entry * 2 + int(run->parity ^ 1u)) * 2;
+    my_ctr = ctrs + (entry * 2 + int(run->parity)) * kStripes * 2;
+    prev_ctr = ctrs + (entry * 2 + int(run->parity ^ 1u)) * kStripes * 2;
   }
   t_in_small_launch = true;
   if (full)
@@ -590,10 +607,15 @@ void set_overlap_small(int on) {
 // CTAs that started early / whose early start the device check withdrew, on the current
 // device since the library was loaded (reads device memory: synchronous).
 int overlap_stats(int64_t* started_early, int64_t* withdrawn) {
-  unsigned long long v[2] = {0, 0};
+  unsigned long long v[kStripes][2] = {};
   if (cudaMemcpyFromSymbol(v, g_overlap_stats, sizeof(v)) != cudaSuccess) return CHOL_ERR_DEVICE;
-  if (started_early) *started_early = int64_t(v[0]);
-  if (withdrawn) *withdrawn = int64_t(v[1]);
+  int64_t e = 0, w = 0;
+  for (int i = 0; i < kStripes; ++i) {
+    e += int64_t(v[i][0]);
+    w += int64_t(v[i][1]);
+  }
+  if (started_early) *started_early = e;
+  if (withdrawn) *withdrawn = w;
   return CHOL_OK;
 }
 

@@ -6,21 +6,28 @@ cholesky/cholesky.py:5692-5802). Here one process per GPU holds the column block
 row-major in a local ``(n, n_local)`` tensor. For every block column ``j``:
 
 1. its owner factors the panel ``L[j*bs:, j*bs:(j+1)*bs]`` in place with one
-   ``chol_panel_potrf_f32`` call (one diagonal-block launch that factors the ``bs x bs`` top
-   block and writes its inverse ``V``, then one tensor-core GEMM ``X = A21 V^T`` that solves
-   every row below);
-2. the factored panel (rows ``j*bs .. n``, ``bs`` columns, at most 32 MiB at n = 32768) is
-   packed contiguously and broadcast by NCCL from the owner into every rank's receive
-   buffer (local memory; no kernel reads another GPU's memory);
-3. every rank applies ``C -= P P^T`` (lower tiles, K = bs) to all of its blocks ``t > j`` in
-   one ``chol_gemm_nt_cyclic_f32`` launch (the GEMM maps local column blocks to their
+   ``chol_panel_potrf_out_f32`` call (one diagonal-block launch that factors the ``bs x bs``
+   top block and writes its inverse ``V``, then one tensor-core GEMM ``X = A21 V^T`` that
+   solves every row below), which also leaves the factored panel (rows ``j*bs .. n``, ``bs``
+   columns, at most 32 MiB at n = 32768) packed contiguously in the send buffer;
+2. NCCL broadcasts it from the owner into every rank's receive buffer (local memory; no
+   kernel reads another GPU's memory);
+3. every rank applies ``C -= P P^T`` (lower tiles) to its blocks right of the look-ahead
+   block with ``chol_gemm_nt_cyclic_f32`` (the GEMM maps local column blocks to their
    global columns, so masking and Q's rows follow the cyclic layout).
 
 Look-ahead: the owner of block ``j+1`` first updates that block with panel ``j``, factors
-it and starts its broadcast; only then does every rank update its remaining blocks with
-panel ``j``, so the broadcast of panel ``j+1`` overlaps the bulk of step ``j``'s update.
-Receive buffers are double-buffered. Every rank issues the same collectives in the same
-order.
+it and starts its broadcast; only then does every rank update its remaining blocks, so the
+broadcast of panel ``j+1`` overlaps the bulk of step ``j``'s update.
+
+Paired updates: the update of the blocks right of the look-ahead block is deferred every
+other step and then applied for two panels at once, ``P = [panel j-1 | panel j]`` (K = 2 bs
+= 512), copied side by side into one buffer. A K = 256 update spends as long in its
+epilogue (the read-modify-write of C) as in its tensor-core main loop; at K = 512 the main
+loop hides it, and the trailing matrix is read and written half as often. The look-ahead
+block still receives every panel before it is factored. Receive buffers rotate over three
+panels (the deferred one, the current one and the one in flight). Every rank issues the
+same collectives in the same order.
 
 The arithmetic goes through an ``ops`` object: ``CudaOps`` (the C ABI of libchol_b200.so,
 the product path). Tests substitute a CPU implementation to check the schedule with
@@ -116,6 +123,20 @@ class CudaOps:
             ctypes.c_void_p(info.data_ptr()) if info is not None else None, self._q())
         _lib.check(st, "chol_block_potrf_f32")
 
+    def panel_potrf_out(self, panel: torch.Tensor, out: torch.Tensor,
+                        info: torch.Tensor | None) -> bool:
+        """Factor a tall panel view in place and write it to ``out`` (m x w, contiguous) as
+        well. False when the one-launch form does not take the shape (nothing done)."""
+        m, w = panel.shape
+        st = self.lib.chol_panel_potrf_out_f32(
+            ctypes.c_void_p(panel.data_ptr()), _rowmajor(panel), m, w,
+            ctypes.c_void_p(out.data_ptr()),
+            ctypes.c_void_p(info.data_ptr()) if info is not None else None, self._q())
+        if st == _lib.CHOL_ERR_UNSUPPORTED:
+            return False
+        _lib.check(st, "chol_panel_potrf_out_f32")
+        return True
+
     def panel_potrf(self, panel: torch.Tensor, tinv: torch.Tensor, info: torch.Tensor | None):
         """Factor a tall panel view (m x w, element (0,0) on the diagonal) in place."""
         m, w = panel.shape
@@ -157,30 +178,40 @@ class CudaOps:
         _lib.check(st, "chol_gemm_nt_f32")
 
 
-def _factor_panel(local: torch.Tensor, lay: CyclicLayout, t: int, ops, tinv, info):
-    """Owner: factor block column t in place (rows t*bs..n of its local columns)."""
+def _factor_panel(local: torch.Tensor, lay: CyclicLayout, t: int, ops, tinv, info, out=None):
+    """Owner: factor block column t in place (rows t*bs..n of its local columns); with
+    ``out`` (rows x width, contiguous) the factored panel is also left there."""
     c0, w, lc = t * lay.bs, lay.width(t), lay.local_col(t)
-    ops.panel_potrf(local[c0:, lc:lc + w], tinv, info)
+    view = local[c0:, lc:lc + w]
+    fused = getattr(ops, "panel_potrf_out", None)
+    if out is not None and fused is not None and fused(view, out, info):
+        return
+    ops.panel_potrf(view, tinv, info)
+    if out is not None:
+        out.copy_(view)
 
 
-def _update_blocks(local: torch.Tensor, lay: CyclicLayout, blocks: list[int], j: int, panel,
-                   ops):
-    """Owned blocks `blocks` (consecutive in this rank's storage) -= panel_j P P^T, lower
-    part, in one call: local column block b stands for global block blocks[0] + b*world."""
+def _update_blocks(local: torch.Tensor, lay: CyclicLayout, blocks: list[int], first_row: int,
+                   panel, ops):
+    """Owned blocks `blocks` (consecutive in this rank's storage) -= P P^T, lower part, in one
+    call, where P = panel's rows from the blocks' first row (panel row 0 is global row
+    first_row): local column block b stands for global block blocks[0] + b*world."""
     bs = lay.bs
     t0 = blocks[0]
     c0, lc0 = t0 * bs, lay.local_col(t0)
     width = sum(lay.width(t) for t in blocks)
-    p = panel[c0 - j * bs:]
+    p = panel[c0 - first_row:]
     ops.cyclic_update(local[c0:, lc0:lc0 + width], p, bs, bs * lay.world)
 
 
 def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=None, ops=None,
-                        info: torch.Tensor | None = None) -> torch.Tensor:
+                        info: torch.Tensor | None = None, paired: bool = True) -> torch.Tensor:
     """Factor in place the block-column-cyclic matrix whose local columns are ``local``.
 
     ``pg`` is ``torch.distributed`` (or None for a single rank); ``ops`` defaults to
-    ``CudaOps`` on ``local``'s device. Returns ``local`` (now this rank's columns of L).
+    ``CudaOps`` on ``local``'s device. ``paired`` defers every other update of the blocks
+    right of the look-ahead block and applies two panels at once (K = 2 bs). Returns
+    ``local`` (now this rank's columns of L).
     """
     if ops is None:
         ops = CudaOps(local.device)
@@ -188,40 +219,56 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
     nb = lay.nblocks
     dev = local.device
     tinv = torch.zeros(64, 64, dtype=local.dtype, device=dev)
-    bufs = [torch.empty(n * bs, dtype=local.dtype, device=dev) for _ in range(2)]
+    paired = paired and nb > 2
+    bufs = [torch.empty(n * bs, dtype=local.dtype, device=dev) for _ in range(3 if paired else 2)]
+    comb = torch.empty(n * 2 * bs, dtype=local.dtype, device=dev) if paired else None
 
     def panel_view(j):
         rows = n - j * bs
-        return bufs[j % 2][: rows * lay.width(j)].view(rows, lay.width(j))
+        return bufs[j % len(bufs)][: rows * lay.width(j)].view(rows, lay.width(j))
 
-    def publish(j):
-        """Owner packs panel j; everyone joins the broadcast. Returns the work handle."""
+    def factor_and_publish(j):
+        """The owner factors block j (fully updated) into the send buffer; every rank joins
+        the broadcast. Returns the work handle."""
         pv = panel_view(j)
         if lay.owner(j) == lay.rank:
-            lc = lay.local_col(j)
-            pv.copy_(local[j * bs:, lc:lc + lay.width(j)])
+            _factor_panel(local, lay, j, ops, tinv, info, out=pv)
         if pg is None or lay.world == 1:
             return None
         return pg.broadcast(pv, src=_global_rank(pg, group, lay.owner(j)), group=group,
                             async_op=True)
 
-    if lay.owner(0) == lay.rank:
-        _factor_panel(local, lay, 0, ops, tinv, info)
-    work = publish(0)
+    work = factor_and_publish(0)
+    pending = None  # panel whose update of the blocks right of the look-ahead is deferred
     for j in range(nb):
         if work is not None:
             work.wait()
-        panel = panel_view(j)
         nxt = j + 1
         work = None
         if nxt < nb:
             if lay.owner(nxt) == lay.rank:
-                _update_blocks(local, lay, [nxt], j, panel, ops)
-                _factor_panel(local, lay, nxt, ops, tinv, info)
-            work = publish(nxt)
+                if pending is not None:
+                    _update_blocks(local, lay, [nxt], pending * bs, panel_view(pending), ops)
+                _update_blocks(local, lay, [nxt], j * bs, panel_view(j), ops)
+            work = factor_and_publish(nxt)
         rest = [t for t in lay.owned() if t > nxt]
-        if rest:
-            _update_blocks(local, lay, rest, j, panel, ops)
+        if not rest:
+            pending = None
+            continue
+        if paired and pending is None and nxt + 1 < nb:
+            pending = j  # applied together with panel j + 1 at the next step
+            continue
+        if pending is None:
+            _update_blocks(local, lay, rest, j * bs, panel_view(j), ops)
+            continue
+        # P = [panel pending | panel j] over the rows of the blocks being updated
+        r0 = rest[0] * bs
+        rows = n - r0
+        pw = comb[: rows * 2 * bs].view(rows, 2 * bs)
+        pw[:, :bs].copy_(panel_view(pending)[r0 - pending * bs:])
+        pw[:, bs:].copy_(panel_view(j)[r0 - j * bs:])
+        _update_blocks(local, lay, rest, r0, pw, ops)
+        pending = None
     return local
 
 

@@ -59,7 +59,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, n, bs, seed, out_dir):
+def _worker(rank, world, port, n, bs, seed, out_dir, paired=True):
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -69,17 +69,22 @@ def _worker(rank, world, port, n, bs, seed, out_dir):
         a = _matrix(n, seed)
         lay = CyclicLayout(n, world, rank, bs)
         local = scatter_block_cyclic(a, lay)
-        factor_block_cyclic(local, lay, pg=dist, ops=CpuOps())
+        factor_block_cyclic(local, lay, pg=dist, ops=CpuOps(), paired=paired)
         torch.save(local, os.path.join(out_dir, f"part{rank}.pt"))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,n,bs", [(2, 300, 64), (3, 260, 32), (2, 128, 64)])
-def test_block_cyclic_gloo_matches_cholesky(tmp_path, world, n, bs):
+@pytest.mark.parametrize("world,n,bs,paired", [(2, 300, 64, True), (3, 260, 32, True),
+                                               (2, 128, 64, True), (3, 260, 32, False),
+                                               (4, 520, 32, True)])
+def test_block_cyclic_gloo_matches_cholesky(tmp_path, world, n, bs, paired):
+    # paired: every other update of the blocks right of the look-ahead block is deferred
+    # and applied for two panels at once
     port = _free_port()
-    mp.spawn(_worker, args=(world, port, n, bs, 11 + n, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, port, n, bs, 11 + n, str(tmp_path), paired), nprocs=world,
+             join=True)
     parts = [torch.load(tmp_path / f"part{r}.pt") for r in range(world)]
     l = gather_block_cyclic(parts, n, world, bs).double()
     a = _matrix(n, 11 + n).double()

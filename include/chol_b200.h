@@ -171,6 +171,12 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   launch's remaining tasks return; the factor of that call is then invalid. The waits on
  *   the TMA and tensor-core completions of one CTA keep a fixed 2 s bound. */
 #define CHOL_OPT_WAIT_LIMIT_US 9
+/*   CHOL_OPT_CHAIN_WIDTH: block-column width of the left-looking chain that factors one panel
+ *   (n <= 1024) for batches too large for the one-launch path: 128 (default; taken when
+ *   n % 128 == 0 and batch >= 256, else 64) or 64. With 128 each diagonal block is factored and inverted by one launch and
+ *   the chain's GEMMs take 128 columns at a time; it needs 64 KiB more workspace per matrix
+ *   (chol_workspace_bytes includes it; a smaller workspace falls back to 64). */
+#define CHOL_OPT_CHAIN_WIDTH 10
 CHOL_API int chol_set_option(int option, int value);
 
 /*

@@ -34,6 +34,7 @@ CHOL_OPT_PANEL_INVERSE = 6
 CHOL_OPT_OVERLAP_CALLS = 7
 CHOL_OPT_MID_KERNEL = 8
 CHOL_OPT_WAIT_LIMIT_US = 9
+CHOL_OPT_CHAIN_WIDTH = 10
 ENGINE_AUTO, ENGINE_FMA, ENGINE_TENSOR = 0, 1, 2
 
 _i64 = ctypes.c_int64

@@ -57,18 +57,7 @@ def workspace_bytes(batch: int, n: int) -> int:
     return int(_lib.load().chol_workspace_bytes(int(batch), int(n)))
 
 
-_ws_bytes: dict[tuple[int, int], int] = {}
 _one_device: bool | None = None  # a single visible GPU: no device switch is ever needed
-
-
-def _workspace_bytes(lib, batch: int, n: int) -> int:
-    key = (batch, n)
-    need = _ws_bytes.get(key)
-    if need is None:
-        need = int(lib.chol_workspace_bytes(batch, n))
-        if len(_ws_bytes) < 4096:
-            _ws_bytes[key] = need
-    return need
 
 
 def _factor(data: torch.Tensor, want_info: bool):
@@ -92,17 +81,15 @@ def _factor(data: torch.Tensor, want_info: bool):
 
 
 def _launch(lib, data, out, info, batch, n, dev):
-    for attempt in range(2):
-        need = _workspace_bytes(lib, batch, n)
-        ws = torch.empty(need, dtype=torch.uint8, device=data.device) if need else None
-        status = _lib.potrf_ws(
-            data.data_ptr(), out.data_ptr(), batch, n,
-            info.data_ptr() if info is not None else 0,
-            ws.data_ptr() if ws is not None else 0, need, _lib.current_queue(dev))
-        if status != _lib.CHOL_ERR_WORKSPACE or attempt:
-            break
-        # a schedule option changed since the size was cached: ask the library again
-        _ws_bytes.pop((batch, n), None)
+    # the size is asked for on every call (a host-only lookup): it follows the schedule
+    # options, and a workspace sized before an option changed would make the library fall
+    # back to a schedule without its optional regions
+    need = int(lib.chol_workspace_bytes(batch, n)) if n > 64 else 0
+    ws = torch.empty(need, dtype=torch.uint8, device=data.device) if need else None
+    status = _lib.potrf_ws(
+        data.data_ptr(), out.data_ptr(), batch, n,
+        info.data_ptr() if info is not None else 0,
+        ws.data_ptr() if ws is not None else 0, need, _lib.current_queue(dev))
     if status:
         _lib.check(status, "chol_potrf_batched_ws_f32")
     return out, info

@@ -123,10 +123,95 @@ size_t blocked_diag_bytes(int64_t batch, int64_t n) {
   return size_t(batch) * (size_t(nb) * kBlock * kBlock * sizeof(float) + kDiagFlags * sizeof(int)) +
          256;
 }
+// One panel, batches beyond the one-launch crossover, n % 128 == 0: the left-looking chain
+// takes 128-wide block columns (CHOL_OPT_CHAIN_WIDTH, 128 by default), each diagonal block
+// factored with its inverse T (128 x 128 per matrix, this region) by one launch. Against the
+// 64-wide chain: half the launches and half the re-reads of the panel left of each block
+// column (b640n512: 2.75 -> 1.9 GB of traffic per call; 1.31 -> 1.03 ms). One CTA of that
+// block factor takes ~50 us, mostly fetching its unrolled 64 x 64 factor code, so it pays only
+// with several CTAs per SM to overlap: batches of at least kChain128Batch (b60n1024 keeps
+// the 64-wide chain: 0.95 against 0.97 ms).
+int g_chain_width = 128;
+constexpr int64_t kChain128Batch = 256;
+size_t blocked_t128_bytes(int64_t batch, int64_t n) {
+  if (g_chain_width != 128 || n < 256 || n % 128 || outer_width(n) < n || n > 16 * kBlock ||
+      batch < kChain128Batch)
+    return 0;
+  if (blocked_diag_bytes(batch, n)) return 0;  // the one-launch path takes these
+  return size_t(batch) * 128 * 128 * sizeof(float);
+}
 size_t blocked_workspace(int64_t batch, int64_t n) {
   if (use_mid(n)) return 0;
   return blocked_workspace_min(batch, n) + blocked_lo_bytes(batch, n) +
-         blocked_inv_bytes(batch, n) + blocked_diag_bytes(batch, n);
+         blocked_inv_bytes(batch, n) + blocked_diag_bytes(batch, n) +
+         blocked_t128_bytes(batch, n);
+}
+
+// The 128-wide left-looking chain over one panel (reads A directly, like the 64-wide one):
+//   for each block column k (128 wide):
+//     L[k:, k:k+128] = A[k:, k:k+128] - L[k:, 0:k] L[k:k+128, 0:k]^T     (k > 0, lower part)
+//     potrf_block128: L_kk and T_k = inv(L_kk), and the zeros of L's rows right of L_kk
+//     L[k+128:, k:k+128] <- L[k+128:, k:k+128] T_k^T                     (in place; A at k = 0)
+// The solve runs in place: its GEMM tiles are 128 x 128 with K = 128, so each tile reads its
+// whole P block before its epilogue writes the same rows and columns. Returns
+// CHOL_ERR_UNSUPPORTED (nothing launched) when the tensor maps cannot be built.
+int run_chain128(const float* A, float* L, int64_t batch, int64_t n, int* info, float* T128,
+                 cudaStream_t q) {
+  const int64_t mstride = n * n;
+  TcMatrixMaps lm, am, tm;
+  if (!tc_make_matrix_maps(L, n, n, n, batch, mstride, &lm) ||
+      !tc_make_matrix_maps(A, n, n, n, batch, mstride, &am) ||
+      !tc_make_matrix_maps(T128, 128, 128, 128, batch, 128 * 128, &tm))
+    return CHOL_ERR_UNSUPPORTED;
+  int st = CHOL_OK;
+  for (int64_t k = 0; k < n; k += 128) {
+    if (k > 0) {
+      GemmArgs u{};
+      u.C = L + k * n + k;
+      u.Csrc = A + k * n + k;
+      u.cstride = mstride;
+      u.ldc = n;
+      u.P = L + k * n;
+      u.pstride = mstride;
+      u.ldp = n;
+      u.Q = u.P;
+      u.qstride = mstride;
+      u.ldq = n;
+      u.m = n - k;
+      u.ncols = 128;
+      u.K = k;
+      u.alpha = -1.f;
+      u.beta = 1.f;
+      u.lower_only = 1;
+      u.batch = batch;
+      if ((st = launch_gemm_tc_mapped(u, lm, lm, q, true))) return st;
+    }
+    const float* S = k == 0 ? A : L;
+    if ((st = launch_potrf_block128(S, mstride, n, L, mstride, n, batch, k, T128, 128 * 128, 128,
+                                    info, q, n - k - 128)))
+      return st;
+    const int64_t below = n - k - 128;
+    if (below <= 0) continue;
+    GemmArgs x{};
+    x.C = L + (k + 128) * n + k;
+    x.cstride = mstride;
+    x.ldc = n;
+    x.P = S + (k + 128) * n + k;
+    x.pstride = mstride;
+    x.ldp = n;
+    x.Q = T128;
+    x.qstride = 128 * 128;
+    x.ldq = 128;
+    x.m = below;
+    x.ncols = 128;
+    x.K = 128;
+    x.alpha = 1.f;
+    x.beta = 0.f;
+    x.lower_only = 0;
+    x.batch = batch;
+    if ((st = launch_gemm_tc_mapped(x, k == 0 ? am : lm, tm, q, true))) return st;
+  }
+  return CHOL_OK;
 }
 
 // Tensor-core GEMMs of one call share tensor maps built once over L and the inverse blocks;
@@ -222,6 +307,11 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
     if (st) return st;
     return launch_diag_block(L, mstride, n, tblk, int64_t(nb) * kBlock * kBlock, kBlock, nb,
                              false, fl, tk, 1, info, 0, batch, q);
+  }
+  const size_t t128 = blocked_t128_bytes(batch, n);
+  if (t128 && g_gemm_engine != 1 && !use_fused(batch, n) && ws_bytes >= min_bytes + t128) {
+    const int st = run_chain128(A, L, batch, n, info, reinterpret_cast<float*>(ws + min_bytes), q);
+    if (st != CHOL_ERR_UNSUPPORTED) return st;
   }
   BlockedMaps bm;
   TcMatrixMaps lomap, vmap;
@@ -445,6 +535,12 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
 int64_t blocked_launches(int64_t batch, int64_t n, bool fused) {
   if (blocked_diag_bytes(batch, n) && g_panel_inverse == 1 && g_gemm_engine != 1 && !fused)
     return 2;  // copy_lower + diagonal-block kernel
+  if (blocked_t128_bytes(batch, n) && g_gemm_engine != 1 && !fused) {
+    int64_t count = 0;
+    for (int64_t k = 0; k < n; k += 128)
+      count += (k > 0 ? 1 : 0) + 1 + (n - k - 128 > 0 ? 1 : 0);  // update, factor, solve
+    return count;
+  }
   const bool pre = blocked_lo_bytes(batch, n) > 0 && g_gemm_engine != 1;
   const bool inv = pre && g_panel_inverse && blocked_inv_bytes(batch, n) > 0;
   const bool diag_kernel = inv && g_panel_inverse == 1;
@@ -724,6 +820,11 @@ int chol_set_option(int option, int value) {
   if (option == CHOL_OPT_PANEL_INVERSE) {
     if (value < 0 || value > 2) return CHOL_ERR_INVALID_ARG;
     g_panel_inverse = value;
+    return CHOL_OK;
+  }
+  if (option == CHOL_OPT_CHAIN_WIDTH) {
+    if (value != 64 && value != 128) return CHOL_ERR_INVALID_ARG;
+    g_chain_width = value;
     return CHOL_OK;
   }
   if (option == CHOL_OPT_WAIT_LIMIT_US) {

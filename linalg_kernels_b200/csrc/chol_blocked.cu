@@ -66,14 +66,14 @@ int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaSt
 }
 
 // =====================================================================================
-// zero_upper: L[m][i][j] = 0 for j >= 64 * (i / 64 + 1), the part of the strict upper
-// triangle right of each row's 64-wide diagonal block (the diagonal blocks themselves are
-// written whole, zeros included, by potrf_block). Replaces copy_lower when the schedule
+// zero_upper: L[m][i][j] = 0 for j >= bw * (i / bw + 1), the part of the strict upper
+// triangle right of each row's bw-wide diagonal block (the diagonal blocks themselves are
+// written whole, zeros included, by the block factor). Replaces copy_lower when the schedule
 // reads A directly. One thread per 4 consecutive elements (vector path when n % 4 == 0).
 // =====================================================================================
 template <bool VEC>
 __global__ void __launch_bounds__(256) zero_upper_kernel(float* __restrict__ L, int64_t batch,
-                                                         int64_t n) {
+                                                         int64_t n, int64_t bw) {
   griddep_wait();
   griddep_launch();
   const int64_t per_row = VEC ? n / 4 : n;
@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(256) zero_upper_kernel(float* __restrict__ L, 
     const int64_t row_g = t / per_row;
     const int64_t c = (t - row_g * per_row) * (VEC ? 4 : 1);
     const int64_t i = row_g % n;
-    if (c < (i / 64 + 1) * 64) continue;
+    if (c < (i / bw + 1) * bw) continue;
     if (VEC)
       *reinterpret_cast<float4*>(L + row_g * n + c) = make_float4(0.f, 0.f, 0.f, 0.f);
     else
@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(256) zero_upper_kernel(float* __restrict__ L, 
   }
 }
 
-int launch_zero_upper(float* L, int64_t batch, int64_t n, cudaStream_t q, bool pdl) {
+int launch_zero_upper(float* L, int64_t batch, int64_t n, cudaStream_t q, bool pdl, int64_t bw) {
   const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(L) & 15) == 0);
   const int64_t work = batch * n * (vec ? n / 4 : n);
   int64_t blocks = (work + 255) / 256;
@@ -101,9 +101,9 @@ int launch_zero_upper(float* L, int64_t batch, int64_t n, cudaStream_t q, bool p
   if (blocks > int64_t(sms) * 16) blocks = int64_t(sms) * 16;
   if (blocks < 1) blocks = 1;
   cudaError_t e = vec ? launch_pdl(zero_upper_kernel<true>, dim3(unsigned(blocks)), dim3(256), 0,
-                                   q, pdl, L, batch, n)
+                                   q, pdl, L, batch, n, bw)
                       : launch_pdl(zero_upper_kernel<false>, dim3(unsigned(blocks)), dim3(256),
-                                   0, q, pdl, L, batch, n);
+                                   0, q, pdl, L, batch, n, bw);
   return status_from(e);
 }
 
@@ -201,6 +201,234 @@ int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, i
           : launch_pdl(potrf_block_kernel<128>, dim3(unsigned(batch)), dim3(128), 0, q, pdl, S,
                        sstride, lds, L, stride, ld, k, int(kb), Tinv, tstride, tld, info);
   return status_from(e);
+}
+
+// =====================================================================================
+// potrf_block128: one CTA (128 threads) per matrix factors the 128 x 128 block at (k, k) as
+// 2 x 2 blocks of 64 and writes T = inv(L_kk) (128 x 128, lower, zeros above):
+//   L00 = chol(A00), T0 = inv(L00)          (one warp factors; 64 threads invert by columns)
+//   L10 = A10 T0^T
+//   L11 = chol(A11 - L10 L10^T), T1 = inv(L11)
+//   T10 = -T1 (L10 T0)
+// The 64 x 64 products run on FP32 FMA, 4 x 8 outputs per thread. The diagonal block of the
+// 128-wide chain: one launch instead of two 64-wide factors, a GEMM and a solve, and the
+// chain's GEMMs then take 128 columns at a time (half the launches and half the re-reads of
+// the panel left of the block column). S (+ m*sstride, leading dimension lds) is where the
+// block is read (A or L); only its lower part is read. The factor goes to L (+ m*stride, ld)
+// with exact zeros above the diagonal of the block, and with zero_cols > 0 the zeros of
+// L's rows k..k+127 right of the block (zero_cols columns) are written too (the upper part
+// of L that no other step writes; the kernel's own work is latency-bound, so these stores
+// cost little). T (+ m*tstride, leading dimension tld). info[m] as for potrf_block.
+// Shared memory: four 64 x 64 tiles (row stride kPBLD).
+// =====================================================================================
+constexpr int kP2T = 128;  // threads
+constexpr size_t kP2Smem = size_t(4 * 64 * kPBLD + 2 * kPB + kPB) * sizeof(float);
+
+// acc[i][j] += sum_k X[k][4 tr + i] * Y[k][c_j] over the 64 x 64 tiles X, Y (row stride kPBLD),
+// c_j = 4 tc + j (j < 4) and 32 + 4 tc + (j - 4) (j >= 4): each quarter-warp reads 32
+// consecutive floats of a Y row (no bank conflicts). tr = tid >> 3 (0..15), tc = tid & 7.
+__device__ __forceinline__ void p2_fma(float2 (&acc)[4][4], const float* X, const float* Y,
+                                       int tr, int tc) {
+#pragma unroll 4
+  for (int k = 0; k < 64; ++k) {
+    const float4 a = *reinterpret_cast<const float4*>(X + k * kPBLD + 4 * tr);
+    const float4 b0 = *reinterpret_cast<const float4*>(Y + k * kPBLD + 4 * tc);
+    const float4 b1 = *reinterpret_cast<const float4*>(Y + k * kPBLD + 32 + 4 * tc);
+    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 ai = make_float2(av[i], av[i]);
+      acc[i][0] = ffma2(ai, make_float2(b0.x, b0.y), acc[i][0]);
+      acc[i][1] = ffma2(ai, make_float2(b0.z, b0.w), acc[i][1]);
+      acc[i][2] = ffma2(ai, make_float2(b1.x, b1.y), acc[i][2]);
+      acc[i][3] = ffma2(ai, make_float2(b1.z, b1.w), acc[i][3]);
+    }
+  }
+}
+__device__ __forceinline__ int p2_col(int tc, int j) { return j < 2 ? 4 * tc + 2 * j : 32 + 4 * tc + 2 * (j - 2); }
+__device__ __forceinline__ void p2_zero(float2 (&acc)[4][4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
+}
+// this thread's outputs (rows 4 tr + i, columns p2_col(tc, j), +1) to a row-major tile
+// (global with leading dimension ld, or shared with kPBLD), scaled by sign
+__device__ __forceinline__ void p2_store(float* X, int64_t ld, const float2 (&acc)[4][4],
+                                         float sign, int tr, int tc) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float* rp = X + (4 * tr + i) * ld;
+    *reinterpret_cast<float4*>(rp + 4 * tc) =
+        make_float4(sign * acc[i][0].x, sign * acc[i][0].y, sign * acc[i][1].x, sign * acc[i][1].y);
+    *reinterpret_cast<float4*>(rp + 32 + 4 * tc) =
+        make_float4(sign * acc[i][2].x, sign * acc[i][2].y, sign * acc[i][3].x, sign * acc[i][3].y);
+  }
+}
+// ... and transposed into a shared tile: X[c][r] = out[r][c]
+__device__ __forceinline__ void p2_store_t(float* X, const float2 (&acc)[4][4], int tr, int tc) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = p2_col(tc, j);
+    *reinterpret_cast<float4*>(X + c * kPBLD + 4 * tr) =
+        make_float4(acc[0][j].x, acc[1][j].x, acc[2][j].x, acc[3][j].x);
+    *reinterpret_cast<float4*>(X + (c + 1) * kPBLD + 4 * tr) =
+        make_float4(acc[0][j].y, acc[1][j].y, acc[2][j].y, acc[3][j].y);
+  }
+}
+
+// The unrolled factor and column inverse as single non-inlined copies: each runs twice per
+// CTA, and a second inlined copy would be fetched cold from memory like the first.
+__device__ __noinline__ int p2_factor64(float* tile, float* col, float* rdiag, int lane) {
+  return tile64_potrf<kPBLD>(tile, col, rdiag, lane);
+}
+// column c of inv(L) for the factored tile: to dst (+ i * ldd + c, global) and as row c of Tt
+__device__ __noinline__ void p2_inverse_col(const float* tile, const float* rdiag, int c,
+                                            float* dst, int64_t ldd, float* Tt, float* Tr) {
+  float t[kPB];
+  tile64_inverse_column<kPBLD>(tile, rdiag, c, t);
+#pragma unroll
+  for (int i = 0; i < kPB; ++i) {
+    dst[i * ldd + c] = t[i];
+    if (Tr != nullptr) Tr[i * kPBLD + c] = t[i];
+  }
+#pragma unroll
+  for (int i = 0; i < kPB; i += 4)
+    *reinterpret_cast<float4*>(Tt + c * kPBLD + i) = make_float4(t[i], t[i + 1], t[i + 2], t[i + 3]);
+}
+
+__global__ void __launch_bounds__(kP2T, 3)
+    potrf_block128_kernel(const float* __restrict__ S, int64_t sstride, int64_t lds,
+                          float* __restrict__ L, int64_t stride, int64_t ld, int64_t k,
+                          float* __restrict__ T, int64_t tstride, int64_t tld,
+                          int* __restrict__ info, int64_t zero_cols) {
+  extern __shared__ __align__(16) float p2_smem[];
+  float* P0 = p2_smem;
+  float* P1 = P0 + 64 * kPBLD;
+  float* P2 = P1 + 64 * kPBLD;
+  float* P3 = P2 + 64 * kPBLD;
+  float* col = P3 + 64 * kPBLD;
+  float* rdiag = col + 2 * kPB;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int tr = tid >> 3, tc = tid & 7;
+  const int64_t m = blockIdx.x;
+  const float* src = S + m * sstride + k * lds + k;
+  float* dst = L + m * stride + k * ld + k;
+  float* tm = T + m * tstride;
+
+  griddep_wait();
+  griddep_launch();
+
+  // A00 (lower) -> P0; A10 -> P3 transposed (P3[c][r] = A10[r][c]); zeros above the diagonal
+  for (int idx = tid; idx < 64 * 16; idx += kP2T) {
+    const int r = idx >> 4, c4 = (idx & 15) * 4;
+    if (c4 <= r) cp_async16(P0 + r * kPBLD + c4, src + r * lds + c4);
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (64 + r) * lds + c4));
+    P3[(c4 + 0) * kPBLD + r] = v.x;
+    P3[(c4 + 1) * kPBLD + r] = v.y;
+    P3[(c4 + 2) * kPBLD + r] = v.z;
+    P3[(c4 + 3) * kPBLD + r] = v.w;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  for (int idx = tid; idx < 64 * 64; idx += kP2T) {
+    const int r = idx >> 6, c = idx & 63;
+    if (c > r) P0[r * kPBLD + c] = 0.f;
+  }
+  __syncthreads();
+  int f0 = 0;
+  if (tid < 32) f0 = p2_factor64(P0, col, rdiag, lane);
+  __syncthreads();
+  if (tid < 64) {
+    // column c of T0: to global T, row-major to P1 (for L10 T0) and as row c of P2 (T0^T)
+    p2_inverse_col(P0, rdiag, tid, tm, tld, P2, P1);
+  } else {
+    // L00 (and zeros to its right) to L; zeros right of T0 in T
+    for (int idx = tid - 64; idx < 64 * 32; idx += 64) {
+      const int r = idx >> 5, c4 = (idx & 31) * 4;
+      const float4 v = c4 < 64 ? *reinterpret_cast<const float4*>(P0 + r * kPBLD + c4)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(dst + r * ld + c4) = v;
+      if (c4 >= 64) *reinterpret_cast<float4*>(tm + r * tld + c4) = v;
+    }
+  }
+  __syncthreads();
+  // A11 (lower) -> P0 while L10 = A10 T0^T is formed
+  for (int idx = tid; idx < 64 * 16; idx += kP2T) {
+    const int r = idx >> 4, c4 = (idx & 15) * 4;
+    if (c4 <= r) cp_async16(P0 + r * kPBLD + c4, src + (64 + r) * lds + 64 + c4);
+  }
+  float2 acc[4][4];
+  p2_zero(acc);
+  p2_fma(acc, P3, P2, tr, tc);
+  __syncthreads();
+  p2_store(dst + 64 * ld, ld, acc, 1.f, tr, tc);  // L10
+  p2_store_t(P3, acc, tr, tc);                      // P3 = L10^T
+  cp_async_wait_all();
+  __syncthreads();
+  // S11 = A11 - L10 L10^T (lower part, zeros above) in P0
+  p2_zero(acc);
+  p2_fma(acc, P3, P3, tr, tc);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 4 * tr + i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = p2_col(tc, j);
+      float* sp = P0 + r * kPBLD + c;
+      sp[0] = (c <= r) ? sp[0] - acc[i][j].x : 0.f;
+      sp[1] = (c + 1 <= r) ? sp[1] - acc[i][j].y : 0.f;
+    }
+  }
+  __syncthreads();
+  int f1 = 0;
+  if (tid < 32) f1 = p2_factor64(P0, col, rdiag, lane);
+  __syncthreads();
+  if (tid < 64) {
+    // column c of T1: to global T and as row c of P2 (T1^T)
+    p2_inverse_col(P0, rdiag, tid, tm + 64 * tld + 64, tld, P2, nullptr);
+  } else {
+    // L11 to L
+    for (int idx = tid - 64; idx < 64 * 16; idx += 64) {
+      const int r = idx >> 4, c4 = (idx & 15) * 4;
+      *reinterpret_cast<float4*>(dst + (64 + r) * ld + 64 + c4) =
+          *reinterpret_cast<const float4*>(P0 + r * kPBLD + c4);
+    }
+  }
+  // zeros of rows k..k+127 right of the block (streaming stores)
+  for (int64_t idx = tid; idx < 128 * (zero_cols / 4); idx += kP2T) {
+    const int64_t r = idx / (zero_cols / 4), c4 = (idx - r * (zero_cols / 4)) * 4;
+    __stcs(reinterpret_cast<float4*>(dst + r * ld + 128 + c4), make_float4(0.f, 0.f, 0.f, 0.f));
+  }
+  // Y = L10 T0 (P3 = L10^T, P1 = T0 row-major) into P0 once L11 is out
+  p2_zero(acc);
+  p2_fma(acc, P3, P1, tr, tc);
+  __syncthreads();
+  p2_store(P0, kPBLD, acc, 1.f, tr, tc);
+  __syncthreads();
+  // T10 = -T1 Y (P2 = T1^T)
+  p2_zero(acc);
+  p2_fma(acc, P2, P0, tr, tc);
+  p2_store(tm + 64 * tld, tld, acc, -1.f, tr, tc);
+  if (tid == 0 && info != nullptr) {
+    const int f = f0 ? f0 : (f1 ? 64 + f1 : 0);
+    if (k == 0)
+      info[m] = f ? int(k) + f : 0;
+    else if (f && info[m] == 0)
+      info[m] = int(k) + f;
+  }
+}
+
+int launch_potrf_block128(const float* S, int64_t sstride, int64_t lds, float* L, int64_t stride,
+                          int64_t ld, int64_t batch, int64_t k, float* T, int64_t tstride,
+                          int64_t tld, int* info, cudaStream_t q, int64_t zero_cols) {
+  if (batch > 0x7fffffffLL || tld < 128 || lds % 4 || ld % 4 || tld % 4 || zero_cols % 4 ||
+      (reinterpret_cast<uintptr_t>(S) & 15) || (reinterpret_cast<uintptr_t>(L) & 15) ||
+      (reinterpret_cast<uintptr_t>(T) & 15))
+    return CHOL_ERR_UNSUPPORTED;
+  return status_from(launch_pdl(potrf_block128_kernel, dim3(unsigned(batch)), dim3(kP2T), kP2Smem,
+                                q, true, S, sstride, lds, L, stride, ld, k, T, tstride, tld, info,
+                                zero_cols));
 }
 
 // =====================================================================================
@@ -318,6 +546,9 @@ __global__ void __launch_bounds__(128)
 }
 
 cudaError_t prepare_blocked() {
+  cudaError_t e = cudaFuncSetAttribute(potrf_block128_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(kP2Smem));
+  if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(trtri_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               int(trtri_smem(16)));
 }

@@ -171,8 +171,15 @@ void set_overlap_small(int on);
 int overlap_stats(int64_t* started_early, int64_t* withdrawn);
 int launch_copy_lower(const float* A, float* L, int64_t batch, int64_t n, cudaStream_t q,
                       bool pdl);
-// Zeros of L right of each row's 64-wide diagonal block (columns >= 64 * (r / 64 + 1)).
-int launch_zero_upper(float* L, int64_t batch, int64_t n, cudaStream_t q, bool pdl);
+// Zeros of L right of each row's bw-wide diagonal block (columns >= bw * (r / bw + 1)).
+int launch_zero_upper(float* L, int64_t batch, int64_t n, cudaStream_t q, bool pdl,
+                      int64_t bw = 64);
+// 128 x 128 diagonal block at (k, k): factor from S into L and T = inv(L_kk) (128 x 128,
+// leading dimension tld >= 128) in one launch, one 128-thread CTA per matrix; zero_cols
+// zeros of L's rows k..k+127 right of the block are written too.
+int launch_potrf_block128(const float* S, int64_t sstride, int64_t lds, float* L, int64_t stride,
+                          int64_t ld, int64_t batch, int64_t k, float* T, int64_t tstride,
+                          int64_t tld, int* info, cudaStream_t q, int64_t zero_cols);
 // Tinv (+ m * tstride, leading dimension tld) receives inv(L_kk) as a 64 x 64 lower triangle.
 int launch_potrf_block(const float* S, int64_t sstride, int64_t lds, float* L, int64_t stride,
                        int64_t ld, int64_t batch, int64_t k, int64_t kb, float* Tinv, int* info,

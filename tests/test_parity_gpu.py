@@ -332,6 +332,43 @@ def test_mid_kernel_not_spd_info():
     assert want.tolist()[0] == 0 and want.tolist()[3] == 0
 
 
+# One panel, batches beyond the one-launch crossover: the left-looking chain, with 128-wide
+# block columns (the default where n % 128 == 0: potrf_block128 factors and inverts each
+# diagonal block) and with 64-wide ones (CHOL_OPT_CHAIN_WIDTH = 64), for the same inputs.
+@pytest.mark.parametrize("batch,n,lam", [(256, 512, 1e4), (256, 1024, 1e5), (720, 256, 1e3),
+                                         (256, 640, 1e3), (300, 768, 1e4), (96, 512, 1e3)])
+@pytest.mark.parametrize("width", [128, 64])
+def test_chain_widths(batch, n, lam, width):
+    lib = _lib.load()
+    assert batch * float(n) ** 3 > 1.2e10  # past the one-launch crossover
+    assert lib.chol_set_option(_lib.CHOL_OPT_CHAIN_WIDTH, width) == _lib.CHOL_OK
+    try:
+        w = 128 if width == 128 and n % 128 == 0 and batch >= 256 else 64
+        expect = 3 * (n // w) - 2 + (w == 64) if n % w == 0 else None
+        if expect is not None:
+            assert int(lib.chol_launch_count(batch, n)) == expect
+        a, cond = inputs.spectral(batch, n, lam, 8200 + n, device=DEV)
+        _check_input(a, cond)
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_CHAIN_WIDTH, 128)
+
+
+def test_chain128_not_spd_info():
+    """info from the 128-wide chain: the first failing column, in either 64-wide half of a
+    diagonal block, in a later block and in the last column, as LAPACK reports it."""
+    a, _ = inputs.spectral(256, 512, 10.0, 97, device=DEV)
+    a = a.clone()
+    a[1, 10, 10] = -1.0
+    a[2, 100, 100] = -5.0
+    a[4, 300, 300] = -2.0
+    a[6, 511, 511] = -3.0
+    assert int(_lib.load().chol_launch_count(256, 512)) == 10
+    l, info = cholesky_ex(a)
+    want = torch.linalg.cholesky_ex(a.cpu()).info
+    assert torch.equal(info.cpu(), want), (info.cpu()[:8], want[:8])
+    assert int(info.count_nonzero()) == 4
+
+
 def test_single_panel_not_spd_info():
     """info from the one-launch path: the first failing column, as LAPACK reports it."""
     a, _ = inputs.spectral(4, 256, 10.0, 99, device=DEV)

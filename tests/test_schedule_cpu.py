@@ -3,8 +3,10 @@
 chol_launch_count and chol_workspace_bytes are pure host logic; they follow the schedules
 the blocked path picks: one small-kernel launch for n <= 64, one shared-memory-kernel launch
 for n <= 128; for one panel, the whole matrix
-in one diagonal-block launch while batch * n^3 is small, else the 64-wide chain (a zero fill,
-then per 64 columns a factor, a left-looking update and a solve); for several 512-wide
+in one diagonal-block launch while batch * n^3 is small, else the left-looking chain (a zero
+fill, then per block column a factor, a left-looking update and a solve; 128-wide block
+columns when n % 128 == 0, 64-wide otherwise or with CHOL_OPT_CHAIN_WIDTH = 64); for several
+512-wide
 panels, per panel the diagonal block, the solve GEMM, the split and the trailing update.
 Also the reference arm of bench.py (the reference's CPU path) prints its JSON line."""
 
@@ -23,8 +25,10 @@ ROOT = Path(__file__).resolve().parents[1]
 @pytest.mark.parametrize("batch,n,launches", [
     (1, 32, 1), (4096, 32, 1), (1024, 64, 1),
     (4, 256, 2),            # one diagonal-block launch (+ copy)
-    (640, 512, 23),         # chain: zero fill + 8 factors + 7 updates + 7 solves
-    (60, 1024, 47),         # chain: 1 + 16 + 15 + 15
+    (640, 512, 10),         # 128-wide chain: 4 factors (with the zero fill) + 3 updates + 3 solves
+    (60, 1024, 47),         # batch < 256: 64-wide chain: 1 + 16 + 15 + 15
+    (256, 1024, 22),        # 128-wide chain: 8 + 7 + 7
+    (400, 320, 14),         # n % 128 != 0: 64-wide chain: 1 + 5 + 4 + 4
     (3, 200, 11),           # chain with a ragged last block: 1 + 4 + 3 + 3
     (1, 2048, 14),          # 3 x (block, solve, split, trailing) + last block + copy
     (1, 2100, 18),          # 4 full panels + a 52-wide last panel (one factor) + copy
@@ -33,6 +37,18 @@ ROOT = Path(__file__).resolve().parents[1]
 ])
 def test_launch_counts_follow_the_schedule(batch, n, launches):
     assert int(_lib.load().chol_launch_count(batch, n)) == launches
+
+
+def test_chain_width_option():
+    lib = _lib.load()
+    assert lib.chol_set_option(_lib.CHOL_OPT_CHAIN_WIDTH, 96) == _lib.CHOL_ERR_INVALID_ARG
+    assert lib.chol_set_option(_lib.CHOL_OPT_CHAIN_WIDTH, 64) == _lib.CHOL_OK
+    try:
+        assert int(lib.chol_launch_count(640, 512)) == 23   # 64-wide chain: 1 + 8 + 7 + 7
+        assert int(lib.chol_launch_count(256, 1024)) == 47  # 1 + 16 + 15 + 15
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_CHAIN_WIDTH, 128)
+    assert int(lib.chol_launch_count(640, 512)) == 10
 
 
 def test_mid_sizes_take_one_launch_and_no_workspace():
@@ -59,8 +75,10 @@ def test_workspace_regions():
     assert ws(1024, 64) == 0                           # small kernel: no workspace
     # required region: one 64 x 64 inverse block and one counter per matrix
     required = lambda b: b * 64 * 64 * 4 + ((b * 4 + 255) // 256) * 256
-    # one panel, large batch (chain): only the required region
-    assert ws(640, 512) == required(640)
+    # one panel, large batch, n % 128 == 0 (128-wide chain): + one 128 x 128 inverse per matrix
+    assert ws(640, 512) == required(640) + 640 * 128 * 128 * 4
+    # ... n % 128 != 0 (64-wide chain): only the required region
+    assert ws(400, 320) == required(400)
     # one panel, small batch (diagonal-block kernel): + n/64 inverse blocks and the tile
     # flags per matrix, + a ticket counter
     assert ws(4, 256) == required(4) + 4 * (4 * 64 * 64 * 4 + 768 * 4) + 256

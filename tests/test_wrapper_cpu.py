@@ -49,10 +49,10 @@ def test_signature_matches_reference():
     assert params == ["data"]
 
 
-def test_stale_workspace_size_is_asked_again(monkeypatch):
-    """The wrapper caches chol_workspace_bytes per (batch, n); when a schedule option changed
-    since (CHOL_OPT_MID_KERNEL = 0 brings back the blocked schedule's workspace) the library
-    answers CHOL_ERR_WORKSPACE, and the wrapper asks for the size again and retries once."""
+def test_workspace_size_follows_the_options(monkeypatch):
+    """The wrapper asks chol_workspace_bytes on every call: a schedule option that changed
+    between calls (CHOL_OPT_CHAIN_WIDTH, CHOL_OPT_MID_KERNEL) changes the size, and a stale
+    size would make the library fall back to a schedule without its optional regions."""
     from linalg_kernels_b200 import _lib
 
     sizes = iter([0, 4096])
@@ -64,13 +64,12 @@ def test_stale_workspace_size_is_asked_again(monkeypatch):
 
     def fake_potrf(a, l, batch, n, info, ws, ws_bytes, queue):
         calls.append(ws_bytes)
-        return _lib.CHOL_ERR_WORKSPACE if ws_bytes < 4096 else _lib.CHOL_OK
+        return _lib.CHOL_OK
 
     monkeypatch.setattr(_lib, "potrf_ws", fake_potrf)
     monkeypatch.setattr(_lib, "current_queue", lambda dev: 0)
-    monkeypatch.setattr(chol_mod, "_ws_bytes", {})
     data = torch.zeros(3, 100, 100)
     out = torch.empty_like(data)
     chol_mod._launch(FakeLib(), data, out, None, 3, 100, None)
+    chol_mod._launch(FakeLib(), data, out, None, 3, 100, None)
     assert calls == [0, 4096]
-    assert chol_mod._ws_bytes[(3, 100)] == 4096

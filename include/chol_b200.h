@@ -108,10 +108,10 @@ CHOL_API int chol_potrf_batched_ws_f32(const float* A, float* L, int64_t batch, 
  * always allocates its output and workspaces per call. For callers that cannot call
  * cudaMalloc (a host that owns all device memory through its own pool, or a path where
  * cudaMalloc's implicit device synchronisation is not allowed): the caller passes A, L
- * and info as usual, and the scratch comes from a fixed 4 MiB + 1 KiB device array inside
- * the library, held on every GPU that loads the library until exit. A call needs 16 KiB per
- * matrix with n > 128 (the 64 x 64 inverse diagonal blocks of the blocked path) plus its
- * counters, so at most 256 such matrices per call; larger batches return
+ * and info as usual, and the scratch comes from a fixed 4 MiB device array inside the
+ * library, held on every GPU that loads the library until exit. A call needs 16 KiB per
+ * matrix with n > 128 (the 64 x 64 inverse diagonal blocks of the blocked path), so at most
+ * 256 such matrices per call; larger batches return
  * CHOL_ERR_SCRATCH_LIMIT. n <= 128 needs none (with the default options). The optional
  * regions of the blocked schedule are taken from the array when they fit after that.
  * The first call on a device looks up the array's device address with that device
@@ -133,10 +133,8 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   TMA, FP32 FMA otherwise; default), 1 = FP32 FMA only, 2 = tensor cores only.
  */
 #define CHOL_OPT_GEMM_ENGINE 1
-/*   CHOL_OPT_FUSED_PANEL: 1 = one fused launch per 64-wide step of the blocked path (update,
- *   diagonal factor and solve in one tcgen05 kernel), 0 = three launches, -1 = automatic
- *   (default: fused for few large matrices, n > 1024 and one wave of CTAs per step). */
-#define CHOL_OPT_FUSED_PANEL 2
+/*   (Option 2, a fused one-launch 64-wide panel step, was removed: it measured slower than
+ *   the three-launch step for every shape. Setting it returns CHOL_ERR_INVALID_ARG.) */
 /*   CHOL_OPT_OUTER_WIDTH: width of the outer panels of the blocked path (multiple of 64;
  *   0 = default: n for n <= 1024, else 512). */
 #define CHOL_OPT_OUTER_WIDTH 3

@@ -26,7 +26,6 @@ CHOL_ERR_UNSUPPORTED = 7
 CHOL_ERR_SCRATCH_LIMIT = 8
 
 CHOL_OPT_GEMM_ENGINE = 1
-CHOL_OPT_FUSED_PANEL = 2
 CHOL_OPT_OUTER_WIDTH = 3
 CHOL_OPT_LOOKAHEAD = 4
 CHOL_OPT_CHAIN_SMS = 5

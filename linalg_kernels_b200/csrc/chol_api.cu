@@ -83,17 +83,15 @@ bool overlaps_partially(const float* a, const float* b, int64_t count) {
 }
 
 // Workspace of the blocked path: the inverse diagonal blocks (64 x 64 floats per matrix,
-// used by the FP32-FMA schedule and the building blocks) and one arrival counter per matrix
-// for the fused panel step are required. When there is a trailing update (n > outer width
+// used by the 64-wide chain and the FP32-FMA schedule) are required. When there is a
+// trailing update (n > outer width
 // NB, n % 4 == 0) two optional regions follow: the panel buffer (n x NB floats per matrix),
 // which holds the panel solve's output and then the low TF32 parts of the solved panel that
 // the trailing GEMM loads instead of splitting in shared memory, and V = inv(L11) of the
 // panel's NB x NB diagonal block (NB x NB floats per matrix).
 size_t blocked_workspace_min(int64_t batch, int64_t n) {
   if (n <= 64 || use_mid(n)) return 0;
-  const size_t tinv = size_t(batch) * kBlock * kBlock * sizeof(float);
-  const size_t counters = (size_t(batch) * sizeof(unsigned) + 255) & ~size_t(255);
-  return tinv + counters;
+  return size_t(batch) * kBlock * kBlock * sizeof(float);
 }
 size_t blocked_lo_bytes(int64_t batch, int64_t n) {
   const int64_t NB = outer_width(n);
@@ -281,7 +279,6 @@ int g_panel_inverse = 1;
 
 int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, float* Tws,
                 size_t ws_bytes, cudaStream_t q) {
-  unsigned int* counters = reinterpret_cast<unsigned int*>(Tws + batch * kBlock * kBlock);
   const int64_t mstride = n * n;
   const size_t min_bytes = blocked_workspace_min(batch, n);
   const size_t lo_bytes = blocked_lo_bytes(batch, n);
@@ -294,8 +291,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
                  ? reinterpret_cast<float*>(ws + min_bytes + lo_bytes)
                  : nullptr;
   const size_t dg_bytes = blocked_diag_bytes(batch, n);
-  if (dg_bytes && g_panel_inverse == 1 && g_gemm_engine != 1 && !use_fused(batch, n) &&
-      ws_bytes >= min_bytes + dg_bytes) {
+  if (dg_bytes && g_panel_inverse == 1 && g_gemm_engine != 1 && ws_bytes >= min_bytes + dg_bytes) {
     // one panel: the diagonal-block kernel factors the whole matrix in one launch
     const int nb = int(n / kBlock);
     float* tblk = reinterpret_cast<float*>(ws + min_bytes);
@@ -309,18 +305,16 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
                              false, fl, tk, 1, info, 0, batch, q);
   }
   const size_t t128 = blocked_t128_bytes(batch, n);
-  if (t128 && g_gemm_engine != 1 && !use_fused(batch, n) && ws_bytes >= min_bytes + t128) {
+  if (t128 && g_gemm_engine != 1 && ws_bytes >= min_bytes + t128) {
     const int st = run_chain128(A, L, batch, n, info, reinterpret_cast<float*>(ws + min_bytes), q);
     if (st != CHOL_ERR_UNSUPPORTED) return st;
   }
   BlockedMaps bm;
   TcMatrixMaps lomap, vmap;
-  alignas(64) unsigned char pmap[128];
   const int64_t NBw = outer_width(n);
   if (g_gemm_engine != 1)
     bm.ok = tc_make_matrix_maps(L, n, n, n, batch, mstride, &bm.L) &&
-            tc_make_matrix_maps(Tws, kBlock, kBlock, kBlock, batch, kBlock * kBlock, &bm.T) &&
-            panel_make_map(pmap, L, n, batch);
+            tc_make_matrix_maps(Tws, kBlock, kBlock, kBlock, batch, kBlock * kBlock, &bm.T);
   if (!bm.ok || (lo && !tc_make_matrix_maps(lo, n, NBw, NBw, batch, n * NBw, &lomap)))
     lo = nullptr;
   if (!lo || !g_panel_inverse || (V && !tc_make_matrix_maps(V, NBw, NBw, NBw, batch, NBw * NBw,
@@ -337,14 +331,11 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
   std::unique_lock<std::mutex> hold;
   if (sq != nullptr) hold = std::unique_lock<std::mutex>(sq->order);
   int pending = -1, ev = 0, chain_cap = 0;
-  const bool fused = bm.ok && use_fused(batch, n);
-  if (fused && cudaMemsetAsync(counters, 0, size_t(batch) * sizeof(unsigned), q) != cudaSuccess)
-    return CHOL_ERR_LAUNCH;
   // One panel (n <= outer width), 64-wide chain: every block column of L is produced once,
   // so the chain reads A where the copy would be read: the first diagonal block and solve
   // take A, each left-looking update takes its beta * C term from A and writes L, and only
   // the part of L right of the diagonal blocks needs zeros (a third of copy_lower's traffic).
-  const bool from_a = NBw >= n && !fused &&
+  const bool from_a = NBw >= n &&
                       (!bm.ok || tc_make_matrix_maps(A, n, n, n, batch, mstride, &bm.A));
   int st = from_a ? launch_zero_upper(L, batch, n, q, true)
                   : launch_copy_lower(A, L, batch, n, q, true);
@@ -375,13 +366,6 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
       float* Tk = inv ? V + (k - K0) * NBw + (k - K0) : Tws;
       const int64_t tstride = inv ? NBw * NBw : kBlock * kBlock;
       const int64_t tld = inv ? NBw : kBlock;
-      if (fused) {
-        // one fused launch: left-looking update, diagonal factor + inverse, panel solve
-        st = launch_panel_step(pmap, L, n, batch, k, kb, K0, info, counters, q, chain_end,
-                               inv ? Tk : nullptr, tstride, tld);
-        if (st) return st;
-        continue;
-      }
       if (k > K0) {
         // left-looking inside the outer panel: block column k receives the updates of the
         // panel's already factored columns [K0, k) in one GEMM (K = k - K0)
@@ -532,10 +516,10 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
 }
 
 // Launch count of run_blocked for (batch, n); keep in step with the schedule above.
-int64_t blocked_launches(int64_t batch, int64_t n, bool fused) {
-  if (blocked_diag_bytes(batch, n) && g_panel_inverse == 1 && g_gemm_engine != 1 && !fused)
+int64_t blocked_launches(int64_t batch, int64_t n) {
+  if (blocked_diag_bytes(batch, n) && g_panel_inverse == 1 && g_gemm_engine != 1)
     return 2;  // copy_lower + diagonal-block kernel
-  if (blocked_t128_bytes(batch, n) && g_gemm_engine != 1 && !fused) {
+  if (blocked_t128_bytes(batch, n) && g_gemm_engine != 1) {
     int64_t count = 0;
     for (int64_t k = 0; k < n; k += 128)
       count += (k > 0 ? 1 : 0) + 1 + (n - k - 128 > 0 ? 1 : 0);  // update, factor, solve
@@ -554,10 +538,6 @@ int64_t blocked_launches(int64_t batch, int64_t n, bool fused) {
     if (one_launch) count += 1;  // diagonal block + its inverse
     for (int64_t k = K0; !one_launch && k < K0 + KB; k += kBlock) {
       const int64_t kb = (K0 + KB - k) < kBlock ? (K0 + KB - k) : kBlock;
-      if (fused) {
-        count += 1;
-        continue;
-      }
       if (k > K0) count += 1;                  // left-looking panel update
       count += 1;                              // diagonal block
       if (chain_end - k - kb > 0) count += 1;  // panel solve
@@ -677,8 +657,8 @@ int potrf_with_workspace(const float* A, float* L, int64_t batch, int64_t n, int
 }
 
 int prepare_kernels(int /*device*/) {
-  return (prepare_tc() == cudaSuccess && prepare_panel() == cudaSuccess &&
-          prepare_blocked() == cudaSuccess && prepare_mid() == cudaSuccess)
+  return (prepare_tc() == cudaSuccess && prepare_blocked() == cudaSuccess &&
+          prepare_mid() == cudaSuccess)
              ? CHOL_OK
              : CHOL_ERR_DEVICE;
 }
@@ -687,18 +667,6 @@ uint64_t g_wait_limit_ns = 2000000000ull;
 uint64_t wait_limit_ns() { return g_wait_limit_ns; }
 
 int g_gemm_engine = 0;
-// Fused panel step (chol_panel.cu) instead of the three-launch step: 1 always, 0 never,
-// -1 auto. Auto currently means never: measured per step, the fused kernel (one warp factors
-// the diagonal block while five wait, ~28k instructions per CTA) is slower than the three
-// launches (n = 16384: 17.5 vs 16.5 ms; b640n512: 2.85 vs 1.3 ms).
-int g_fused_panel = 0;
-
-bool use_fused(int64_t batch, int64_t n) {
-  if (g_fused_panel >= 0) return g_fused_panel == 1;
-  (void)batch;
-  (void)n;
-  return false;
-}
 
 int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl) {
   if (g.m <= 0 || g.ncols <= 0) return CHOL_OK;
@@ -781,9 +749,7 @@ int chol_potrf_batched_f32(const float* A, float* L, int64_t batch, int64_t n, i
 int64_t chol_launch_count(int64_t batch, int64_t n) {
   if (batch <= 0 || n <= 0) return 0;
   if (n <= 64 || use_mid(n)) return 1;
-  // the fused panel step runs when the tensor-core engine is allowed and rows are
-  // 16-byte multiples (the usual case: n % 4 == 0)
-  return blocked_launches(batch, n, use_fused(batch, n) && g_gemm_engine != 1 && n % 4 == 0);
+  return blocked_launches(batch, n);
 }
 
 int chol_set_option(int option, int value) {
@@ -832,12 +798,7 @@ int chol_set_option(int option, int value) {
     g_wait_limit_ns = value == 0 ? 2000000000ull : uint64_t(value) * 1000ull;
     return CHOL_OK;
   }
-  if (option == CHOL_OPT_FUSED_PANEL) {
-    if (value < -1 || value > 1) return CHOL_ERR_INVALID_ARG;
-    g_fused_panel = value;
-    return CHOL_OK;
-  }
-  return CHOL_ERR_INVALID_ARG;
+  return CHOL_ERR_INVALID_ARG;  // includes option 2, the fused panel step of earlier versions
 }
 
 int chol_overlap_stats(int64_t* started_early, int64_t* withdrawn) {

@@ -237,19 +237,9 @@ uint64_t wait_limit_ns();
 int launch_flag_wait(int* words, int value, cudaStream_t q);
 // Device address of the status word (for kernels in other translation units).
 int* device_status_ptr();
-// Fused 64-wide panel step (chol_panel.cu).
-cudaError_t prepare_panel();
-bool panel_make_map(void* map128, const float* L, int64_t n, int64_t batch);
-// row_end: rows of the panel (default n); tout: optional destination of inv(L_kk).
-int launch_panel_step(const void* map128, float* L, int64_t n, int64_t batch, int64_t k,
-                      int64_t kb, int64_t K0, int* info, unsigned int* counters, cudaStream_t q,
-                      int64_t row_end = 0, float* tout = nullptr, int64_t tstride = 0,
-                      int64_t tld = 0);
 // Engine choice for the NT-GEMM: 0 auto (tensor cores when the operands allow TMA), 1 FP32
 // FMA only, 2 tensor cores only (CHOL_ERR_UNSUPPORTED where TMA cannot be used).
 extern int g_gemm_engine;
-extern int g_fused_panel;
-bool use_fused(int64_t batch, int64_t n);
 int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl);
 
 }  // namespace chol

@@ -6,9 +6,9 @@
 // acceptable. chol_potrf_batched_f32 grows a cached workspace with cudaMalloc, and
 // chol_potrf_batched_ws_f32 needs the caller to allocate one. This entry point instead
 // takes its scratch from one fixed file-scope device array, g_noalloc_scratch, of
-// kNoAllocScratchBytes (4 MiB + 1 KiB). The scratch a call must have (n > 128 only) is the
-// inverse of each 64 x 64 diagonal block of the blocked path, 16 KiB per matrix, plus a
-// 4-byte arrival counter per matrix (rounded up to 256 bytes): at most 256 matrices per call.
+// kNoAllocScratchBytes (4 MiB). The scratch a call must have (n > 128 only) is the inverse
+// of each 64 x 64 diagonal block of the blocked path, 16 KiB per matrix: at most 256
+// matrices per call.
 // The blocked schedule also places its optional regions (the one-launch diagonal-block
 // buffers, the panel buffer of precomputed low parts, V = inv(L11)) in the array when they
 // fit after that, and runs without them otherwise. Every GPU that loads the library holds
@@ -20,7 +20,7 @@
 // first call should therefore come before any stream capture.
 //
 // All calls share the one array and it keeps the previous call's contents. The regions
-// that must start at zero (counters, tile flags, tickets) are cleared by every call on its
+// that must start at zero (tile flags, tickets) are cleared by every call on its
 // queue (cudaMemsetAsync); the inverse blocks are written before they are read,
 // but calls whose work overlaps on the GPU (different queues, or different host threads
 // without ordering) race on it and must be serialised by the caller.
@@ -31,8 +31,8 @@
 namespace chol {
 namespace {
 
-// 256 matrices with n > 128: 4 MiB of inverse blocks + 1 KiB of per-matrix counters
-constexpr size_t kNoAllocScratchBytes = (size_t(4) << 20) + (size_t(1) << 10);
+// 256 matrices with n > 128: 4 MiB of inverse blocks
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

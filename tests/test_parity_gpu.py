@@ -240,16 +240,8 @@ def test_building_blocks_against_torch():
     assert (l[:, kb:, :kb] - want_x).abs().max().item() < 1e-4
 
 
-@pytest.mark.parametrize("name", ["b64n256", "b640n512", "b60n1024"])
-def test_fused_panel_step_option(name):
-    """The fused one-launch panel step (CHOL_OPT_FUSED_PANEL) gives a factor within the
-    same bounds as the default three-launch step."""
-    lib = _lib.load()
-    lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, 1)
-    try:
-        _check_full_config(name, batch=8)
-    finally:
-        lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, -1)
+def test_removed_fused_panel_option_is_rejected():
+    assert _lib.load().chol_set_option(2, 1) == _lib.CHOL_ERR_INVALID_ARG
 
 
 def test_row_chain_panel_solve_at_large_n():
@@ -268,17 +260,15 @@ def test_row_chain_panel_solve_at_large_n():
 # panel buffer). Spectral inputs up to cond 1e5 exercise the inverse-based panel solve.
 @pytest.mark.parametrize("batch,n,lam", [(1, 1536, 1e3), (3, 2048, 1e4), (1, 2100, 1e5),
                                          (2, 1030, 1e3), (1, 2050, 1e4), (1, 4096, 1e5)])
-@pytest.mark.parametrize("panel_inverse,fused", [(1, 0), (2, 0), (0, 0), (2, 1)])
-def test_multi_panel_sizes(batch, n, lam, panel_inverse, fused):
+@pytest.mark.parametrize("panel_inverse", [1, 2, 0])
+def test_multi_panel_sizes(batch, n, lam, panel_inverse):
     lib = _lib.load()
     lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, panel_inverse)
-    lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, fused)
     try:
         a, cond = inputs.spectral(batch, n, lam, 7000 + n, device=DEV)
         _check_input(a, cond)
     finally:
         lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)
-        lib.chol_set_option(_lib.CHOL_OPT_FUSED_PANEL, -1)
 
 
 # n <= 1024, n % 64 == 0, small batch: the whole matrix in one diagonal-block launch (FP32

@@ -73,8 +73,8 @@ def test_workspace_regions():
     lib = _lib.load()
     ws = lambda b, n: int(lib.chol_workspace_bytes(b, n))
     assert ws(1024, 64) == 0                           # small kernel: no workspace
-    # required region: one 64 x 64 inverse block and one counter per matrix
-    required = lambda b: b * 64 * 64 * 4 + ((b * 4 + 255) // 256) * 256
+    # required region: one 64 x 64 inverse block per matrix
+    required = lambda b: b * 64 * 64 * 4
     # one panel, large batch, n % 128 == 0 (128-wide chain): + one 128 x 128 inverse per matrix
     assert ws(640, 512) == required(640) + 640 * 128 * 128 * 4
     # ... n % 128 != 0 (64-wide chain): only the required region

@@ -238,6 +238,14 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
         return pg.broadcast(pv, src=_global_rank(pg, group, lay.owner(j)), group=group,
                             async_op=True)
 
+    def combined(p, j, r0):
+        """[panel p | panel j] over the global rows r0..n, side by side in one buffer."""
+        rows = n - r0
+        pw = comb[: rows * 2 * bs].view(rows, 2 * bs)
+        pw[:, :bs].copy_(panel_view(p)[r0 - p * bs:])
+        pw[:, bs:].copy_(panel_view(j)[r0 - j * bs:])
+        return pw
+
     work = factor_and_publish(0)
     pending = None  # panel whose update of the blocks right of the look-ahead is deferred
     for j in range(nb):
@@ -245,29 +253,30 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
             work.wait()
         nxt = j + 1
         work = None
-        if nxt < nb:
-            if lay.owner(nxt) == lay.rank:
-                if pending is not None:
-                    _update_blocks(local, lay, [nxt], pending * bs, panel_view(pending), ops)
-                _update_blocks(local, lay, [nxt], j * bs, panel_view(j), ops)
-            work = factor_and_publish(nxt)
         rest = [t for t in lay.owned() if t > nxt]
+        owns_next = nxt < nb and lay.owner(nxt) == lay.rank
+        pw = None
+        if pending is not None and (rest or owns_next):
+            # P = [panel pending | panel j] from the look-ahead block's first row down: one
+            # K = 2 bs update for the look-ahead block and one for the blocks right of it
+            pw = combined(pending, j, nxt * bs)
+        if nxt < nb:
+            if owns_next:
+                if pw is not None:
+                    _update_blocks(local, lay, [nxt], nxt * bs, pw, ops)
+                else:
+                    _update_blocks(local, lay, [nxt], j * bs, panel_view(j), ops)
+            work = factor_and_publish(nxt)
         if not rest:
             pending = None
             continue
         if paired and pending is None and nxt + 1 < nb:
             pending = j  # applied together with panel j + 1 at the next step
             continue
-        if pending is None:
+        if pw is None:
             _update_blocks(local, lay, rest, j * bs, panel_view(j), ops)
-            continue
-        # P = [panel pending | panel j] over the rows of the blocks being updated
-        r0 = rest[0] * bs
-        rows = n - r0
-        pw = comb[: rows * 2 * bs].view(rows, 2 * bs)
-        pw[:, :bs].copy_(panel_view(pending)[r0 - pending * bs:])
-        pw[:, bs:].copy_(panel_view(j)[r0 - j * bs:])
-        _update_blocks(local, lay, rest, r0, pw, ops)
+        else:
+            _update_blocks(local, lay, rest, nxt * bs, pw, ops)
         pending = None
     return local
 

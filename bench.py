@@ -1006,6 +1006,10 @@ def run_ncu_target(args):
 
     cfg = inputs.GRID[args.config]
     dev = torch.device("cuda", 0)
+    if not args.overlap:
+        from linalg_kernels_b200 import _lib
+
+        _lib.load().chol_set_option(_lib.CHOL_OPT_OVERLAP_CALLS, 0)
     gen_dev = "cpu" if cfg.n <= 1024 else dev
     a, _ = inputs.config_input(cfg, device=gen_dev)
     a = a.to(dev)
@@ -1041,6 +1045,10 @@ def main(argv=None):
     ap.add_argument("--probe", default=None,
                     help="time the tensor-core GEMM alone in the given roles "
                          "(comma list of trailing,inpanel,solve) and exit")
+    ap.add_argument("--overlap", action=argparse.BooleanOptionalAction, default=True,
+                    help="with --ncu-run: --no-overlap makes every n <= 64 call wait for the "
+                         "one before it (CHOL_OPT_OVERLAP_CALLS = 0), the single-launch case "
+                         "a serialising profiler sees anyway")
     ap.add_argument("--ncu-run", action="store_true",
                     help="only call custom_kernel warmup + steps times on one input of --config "
                          "(the target of the ncu captures in profiles/)")

@@ -141,7 +141,10 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
 /*   CHOL_OPT_LOOKAHEAD: 1 = for large n, most of the trailing update of an outer panel runs
  *   on a library side queue beside the next panel's factorisation, for the panels whose
  *   update is short enough for the overlap to pay (the call still completes on the
- *   caller's queue); 0 (default) = everything in order on the caller's queue.
+ *   caller's queue); 0 = everything in order on the caller's queue; -1 (default) = 1 for
+ *   1024 < n <= 8192, else 0. The side queue is shared by the calls on a device (they take
+ *   turns through a lock), so a call that uses it cannot be captured into a CUDA graph;
+ *   set 0 before capturing such calls.
  *   CHOL_OPT_CHAIN_SMS: SMs the side-queue update leaves free for the panel chain (24). */
 #define CHOL_OPT_LOOKAHEAD 4
 #define CHOL_OPT_CHAIN_SMS 5

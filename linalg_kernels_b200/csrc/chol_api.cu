@@ -234,13 +234,20 @@ int gemm_on(const GemmArgs& g, const BlockedMaps& bm, const TcMatrixMaps& pm,
 // diagonal block, panel solve and split then run beside T2. The cap slows T2 by about
 // sms / (sms - g_chain_sms), so the split is taken only while T2 is short enough for the
 // overlap to win: batch * rest^2 <= kLookaheadWork (rest = rows below the next panel; about
-// 1 ms of T2 on a B200 against ~0.2 ms of per-panel chain).
-int g_lookahead = 0;
+// 1 ms of T2 on a B200 against ~0.2 ms of per-panel chain). Automatic (-1, the default):
+// on for n <= kLookaheadAutoN, where it measured faster (b1n4096 1.41 -> 1.38 ms, b2n4096
+// 1.55 -> 1.49, b1n8192 3.58 -> 3.29); at n = 16384 the capped T2 costs more than the
+// overlap wins (12.80 against 12.72 ms), so it stays off there.
+int g_lookahead = -1;
 int g_chain_sms = 24;
 constexpr double kLookaheadWork = 4.0e8;
+constexpr int64_t kLookaheadAutoN = 8192;
 
-bool lookahead_split(int64_t batch, int64_t rest_after_next) {
-  return g_lookahead && rest_after_next > 0 &&
+bool lookahead_on(int64_t n) {
+  return g_lookahead == 1 || (g_lookahead < 0 && n <= kLookaheadAutoN);
+}
+bool lookahead_split(int64_t batch, int64_t n, int64_t rest_after_next) {
+  return lookahead_on(n) && rest_after_next > 0 &&
          double(batch) * double(rest_after_next) * double(rest_after_next) <= kLookaheadWork;
 }
 
@@ -327,7 +334,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
   if (inv && cudaMemsetAsync(V, 0, inv_bytes, q) != cudaSuccess) return CHOL_ERR_LAUNCH;
   int dev = 0;
   cudaGetDevice(&dev);
-  SideQueue* sq = (lo != nullptr && g_lookahead) ? side_queue(dev) : nullptr;
+  SideQueue* sq = (lo != nullptr && lookahead_on(n)) ? side_queue(dev) : nullptr;
   std::unique_lock<std::mutex> hold;
   if (sq != nullptr) hold = std::unique_lock<std::mutex>(sq->order);
   int pending = -1, ev = 0, chain_cap = 0;
@@ -483,7 +490,7 @@ int run_blocked(const float* A, float* L, int64_t batch, int64_t n, int* info, f
     if (st) return st;
     const int64_t K0n = K0 + KB;
     const int64_t KBn = rest < NBw ? rest : NBw;
-    if (sq != nullptr && rest > KBn && lookahead_split(batch, rest - KBn)) {
+    if (sq != nullptr && rest > KBn && lookahead_split(batch, n, rest - KBn)) {
       // T1: next panel's columns, here; T2: the rest, on the side queue
       GemmArgs t1 = t;
       t1.ncols = KBn;
@@ -549,7 +556,7 @@ int64_t blocked_launches(int64_t batch, int64_t n) {
     }
     count += inv ? (one_launch ? 2 : 3) : 1;     // ((trtri +) solve GEMM +) split/lo pass
     count += 1;                                  // trailing update
-    if (rest > NB && lookahead_split(batch, rest - NB)) count += 1;  // T1 + T2
+    if (rest > NB && lookahead_split(batch, n, rest - NB)) count += 1;  // T1 + T2
   }
   return count;
 }
@@ -764,7 +771,7 @@ int chol_set_option(int option, int value) {
     return CHOL_OK;
   }
   if (option == CHOL_OPT_LOOKAHEAD) {
-    if (value < 0 || value > 1) return CHOL_ERR_INVALID_ARG;
+    if (value < -1 || value > 1) return CHOL_ERR_INVALID_ARG;
     g_lookahead = value;
     return CHOL_OK;
   }

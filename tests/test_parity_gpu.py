@@ -386,5 +386,5 @@ def test_lookahead_matches_in_order_schedule(n):
             torch.cuda.synchronize()
             assert torch.equal(got, want), inv
     finally:
-        lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 0)
+        lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, -1)
         lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)

@@ -30,13 +30,27 @@ ROOT = Path(__file__).resolve().parents[1]
     (256, 1024, 22),        # 128-wide chain: 8 + 7 + 7
     (400, 320, 14),         # n % 128 != 0: 64-wide chain: 1 + 5 + 4 + 4
     (3, 200, 11),           # chain with a ragged last block: 1 + 4 + 3 + 3
-    (1, 2048, 14),          # 3 x (block, solve, split, trailing) + last block + copy
-    (1, 2100, 18),          # 4 full panels + a 52-wide last panel (one factor) + copy
+    (1, 2048, 16),          # 3 x (block, solve, split, trailing) + last block + copy,
+                            # + 2 look-ahead splits (automatic for n <= 8192)
+    (1, 2100, 21),          # 4 full panels + a 52-wide last panel (one factor) + copy + 3 splits
     (1, 16384, 126),        # 31 x 4 + last block + copy
     (2, 1030, 50),          # rows not 16-byte multiples: the 64-wide steps in each panel
 ])
 def test_launch_counts_follow_the_schedule(batch, n, launches):
     assert int(_lib.load().chol_launch_count(batch, n)) == launches
+
+
+def test_lookahead_option():
+    lib = _lib.load()
+    assert lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 2) == _lib.CHOL_ERR_INVALID_ARG
+    try:
+        assert lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 0) == _lib.CHOL_OK
+        assert int(lib.chol_launch_count(1, 2048)) == 14
+        assert lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 1) == _lib.CHOL_OK
+        assert int(lib.chol_launch_count(1, 16384)) > 126
+    finally:
+        lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, -1)
+    assert int(lib.chol_launch_count(1, 16384)) == 126   # automatic: off above n = 8192
 
 
 def test_chain_width_option():

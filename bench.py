@@ -57,7 +57,7 @@ REFERENCE_PUBLISHED_S = {
 # same workload (python bench.py --ncu-run --config <name>; the short summaries live in the
 # profiles folder). None until captured.
 NCU_TRAFFIC_BYTES: dict[str, float | None] = {
-    "b1024n64": 12.72e6,   # small_potrf_kernel; its writes are still in L2 at kernel end
+    "b1024n64": 12.74e6,   # small_potrf_kernel; its writes are still in L2 at kernel end
     "b4096n32": 16.80e6,   # small_potrf_kernel; likewise
 }
 

@@ -261,10 +261,13 @@ CHOL_API int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, fl
 /* chol_panel_potrf_f32 (the one-launch form: w a multiple of 64, <= 1024, 16-byte aligned
    rows) that also writes the factored panel to out: m x w floats, row-major, contiguous,
    disjoint from L. The panel solve writes its rows straight into out, so the multi-GPU
-   driver sends out without packing the panel first. CHOL_ERR_UNSUPPORTED for shapes the
-   one-launch form does not take. */
+   driver sends out without packing the panel first. With flags = CHOL_PANEL_OUT_ONLY the
+   solved rows below the w x w top block are left in out only (L receives the top block);
+   the caller copies them into L, e.g. beside the send. flags = 0: L receives the whole
+   factored panel too. CHOL_ERR_UNSUPPORTED for shapes the one-launch form does not take. */
+#define CHOL_PANEL_OUT_ONLY 1
 CHOL_API int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w, float* out,
-                                      int* info, void* queue);
+                                      int flags, int* info, void* queue);
 
 /* chol_gemm_nt_f32 for one matrix whose columns are stored block-cyclically: local column c
    of C (and row c of Q) stands for global column c + (c / col_block) * (col_stride -

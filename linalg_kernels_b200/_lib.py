@@ -24,6 +24,7 @@ CHOL_ERR_WORKSPACE = 5
 CHOL_ERR_DEVICE = 6
 CHOL_ERR_UNSUPPORTED = 7
 CHOL_ERR_SCRATCH_LIMIT = 8
+CHOL_PANEL_OUT_ONLY = 1
 
 CHOL_OPT_GEMM_ENGINE = 1
 CHOL_OPT_OUTER_WIDTH = 3
@@ -61,7 +62,7 @@ SIGNATURES: dict[str, tuple] = {
     "chol_gemm_nt_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64,
                                 _vp, _i64, _i64, _f32, _f32, _i64, _int, _vp]),
     "chol_panel_potrf_f32": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
-    "chol_panel_potrf_out_f32": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "chol_panel_potrf_out_f32": (_int, [_vp, _i64, _i64, _i64, _vp, _int, _vp, _vp]),
     "chol_gemm_nt_cyclic_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _f32,
                                        _f32, _i64, _int, _i64, _i64, _vp]),
     "chol_validate_work_bytes": (_sz, [_i64, _i64]),

@@ -611,7 +611,7 @@ void* panel_scratch(int dev, size_t need) {
 // With out != nullptr the solve writes X straight into rows w.. of out (m x w, row-major,
 // contiguous), and the top block is copied there too: the packed panel, ready to send.
 int panel_potrf_inverse(float* L, int64_t ld, int64_t m, int64_t w, int* info, int dev,
-                        cudaStream_t q, float* out = nullptr) {
+                        cudaStream_t q, float* out = nullptr, bool copy_back = true) {
   const int nb = int(w / kBlock);
   const size_t vbytes = size_t(w) * size_t(w) * sizeof(float);
   const size_t fbytes = kDiagFlags * sizeof(int) + 256;
@@ -646,6 +646,7 @@ int panel_potrf_inverse(float* L, int64_t ld, int64_t m, int64_t w, int* info, i
   x.beta = 0.f;
   x.batch = 1;
   if ((st = launch_gemm(x, q, true))) return st;
+  if (!copy_back) return CHOL_OK;  // the caller copies out's rows w.. into L itself
   return launch_tf32_lo(X, w, scratch_x, w, m - w, w, 1, 0, 0, q, L + w * ld, ld, 0);
 }
 
@@ -947,8 +948,9 @@ int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv
   return CHOL_OK;
 }
 
-int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w, float* out, int* info,
-                             void* queue) {
+int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w, float* out, int flags,
+                             int* info, void* queue) {
+  if (flags & ~CHOL_PANEL_OUT_ONLY) return CHOL_ERR_INVALID_ARG;
   if (L == nullptr || out == nullptr || m < 0 || w < 0 || w > m || ld < w)
     return CHOL_ERR_INVALID_ARG;
   if (m == 0 || w == 0) return CHOL_OK;
@@ -961,7 +963,8 @@ int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w, float* 
   int dev = 0, st;
   if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
   if ((st = prepare_device(dev))) return st;
-  return panel_potrf_inverse(L, ld, m, w, info, dev, static_cast<cudaStream_t>(queue), out);
+  return panel_potrf_inverse(L, ld, m, w, info, dev, static_cast<cudaStream_t>(queue), out,
+                             (flags & CHOL_PANEL_OUT_ONLY) == 0);
 }
 
 int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t ncols, int64_t K,

@@ -124,13 +124,15 @@ class CudaOps:
         _lib.check(st, "chol_block_potrf_f32")
 
     def panel_potrf_out(self, panel: torch.Tensor, out: torch.Tensor,
-                        info: torch.Tensor | None) -> bool:
+                        info: torch.Tensor | None, out_only: bool = False) -> bool:
         """Factor a tall panel view in place and write it to ``out`` (m x w, contiguous) as
-        well. False when the one-launch form does not take the shape (nothing done)."""
+        well; with ``out_only`` the rows below the w x w top block stay in ``out`` only (the
+        caller copies them into ``panel``). False when the one-launch form does not take the
+        shape (nothing done)."""
         m, w = panel.shape
         st = self.lib.chol_panel_potrf_out_f32(
             ctypes.c_void_p(panel.data_ptr()), _rowmajor(panel), m, w,
-            ctypes.c_void_p(out.data_ptr()),
+            ctypes.c_void_p(out.data_ptr()), _lib.CHOL_PANEL_OUT_ONLY if out_only else 0,
             ctypes.c_void_p(info.data_ptr()) if info is not None else None, self._q())
         if st == _lib.CHOL_ERR_UNSUPPORTED:
             return False
@@ -178,17 +180,24 @@ class CudaOps:
         _lib.check(st, "chol_gemm_nt_f32")
 
 
-def _factor_panel(local: torch.Tensor, lay: CyclicLayout, t: int, ops, tinv, info, out=None):
+def _factor_panel(local: torch.Tensor, lay: CyclicLayout, t: int, ops, tinv, info, out=None,
+                  defer_copy: bool = False):
     """Owner: factor block column t in place (rows t*bs..n of its local columns); with
-    ``out`` (rows x width, contiguous) the factored panel is also left there."""
+    ``out`` (rows x width, contiguous) the factored panel is also left there. With
+    ``defer_copy`` the rows below the top block may be left in ``out`` only: the return value
+    is then the (destination, source) pair still to copy, else None."""
     c0, w, lc = t * lay.bs, lay.width(t), lay.local_col(t)
     view = local[c0:, lc:lc + w]
     fused = getattr(ops, "panel_potrf_out", None)
-    if out is not None and fused is not None and fused(view, out, info):
-        return
+    if out is not None and fused is not None:
+        if defer_copy and view.shape[0] > w and fused(view, out, info, out_only=True):
+            return view[w:], out[w:]
+        if fused(view, out, info):
+            return None
     ops.panel_potrf(view, tinv, info)
     if out is not None:
         out.copy_(view)
+    return None
 
 
 def _update_blocks(local: torch.Tensor, lay: CyclicLayout, blocks: list[int], first_row: int,
@@ -229,14 +238,20 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
 
     def factor_and_publish(j):
         """The owner factors block j (fully updated) into the send buffer; every rank joins
-        the broadcast. Returns the work handle."""
+        the broadcast. The owner copies the solved rows back into its own columns after the
+        broadcast is issued, so that copy runs beside the send instead of before it. Returns
+        the work handle."""
         pv = panel_view(j)
+        back = None
         if lay.owner(j) == lay.rank:
-            _factor_panel(local, lay, j, ops, tinv, info, out=pv)
-        if pg is None or lay.world == 1:
-            return None
-        return pg.broadcast(pv, src=_global_rank(pg, group, lay.owner(j)), group=group,
-                            async_op=True)
+            back = _factor_panel(local, lay, j, ops, tinv, info, out=pv, defer_copy=True)
+        handle = None
+        if pg is not None and lay.world > 1:
+            handle = pg.broadcast(pv, src=_global_rank(pg, group, lay.owner(j)), group=group,
+                                  async_op=True)
+        if back is not None:
+            back[0].copy_(back[1])
+        return handle
 
     def combined(p, j, r0):
         """[panel p | panel j] over the global rows r0..n, side by side in one buffer."""

@@ -1,6 +1,8 @@
 """GPU: the block-column-cyclic driver with the CUDA ops on one rank (no process group):
 the same schedule the multi-GPU path runs, checked against the oracle's bounds."""
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -209,3 +211,34 @@ def test_panel_potrf_reports_not_spd():
     CudaOps(torch.device(DEV)).panel_potrf(panel[:, :w], tinv, info)
     torch.cuda.synchronize()
     assert int(info.item()) == 131
+
+
+@pytest.mark.parametrize("m,w", [(3000, 256), (512, 256), (1500, 128)])
+def test_panel_potrf_out_flags(m, w):
+    """chol_panel_potrf_out_f32: the factored panel in the contiguous send buffer equals the
+    panel factored in place by chol_panel_potrf_f32 (the same kernels, bitwise); with
+    CHOL_PANEL_OUT_ONLY, L receives the top block only and the rows below stay as they were
+    (the multi-GPU driver copies them back beside the send)."""
+    from linalg_kernels_b200 import _lib
+    from linalg_kernels_b200.distributed import CudaOps
+
+    lib = _lib.load()
+    ops = CudaOps(torch.device(DEV))
+    a, _ = inputs.covariance(1, m, 0.5, 77 * m + w)
+    base = torch.tril(a[0]).to(DEV).contiguous()
+    ref = base.clone()
+    ops.panel_potrf(ref[:, :w], torch.empty(64, 64, device=DEV), None)
+    for out_only in (False, True):
+        panel = base.clone()
+        out = torch.full((m, w), float("nan"), device=DEV)
+        assert ops.panel_potrf_out(panel[:, :w], out, None, out_only=out_only)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref[:, :w])
+        assert torch.equal(panel[:w, :w], ref[:w, :w])
+        if out_only:
+            assert torch.equal(panel[w:, :w], base[w:, :w])
+        else:
+            assert torch.equal(panel[:, :w], ref[:, :w])
+    st = lib.chol_panel_potrf_out_f32(ctypes.c_void_p(base.data_ptr()), m, m, w,
+                                      ctypes.c_void_p(out.data_ptr()), 2, None, None)
+    assert st == _lib.CHOL_ERR_INVALID_ARG

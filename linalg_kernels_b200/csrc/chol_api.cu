@@ -26,13 +26,20 @@ namespace {
 
 constexpr int64_t kBlock = 64;
 
-int g_outer_width = 0;  // 0: default (n for n <= 1024, else 512)
+int g_outer_width = 0;  // 0: default (below)
 
+// n <= 1024: one outer panel. Larger: panels of width NB with a rank-NB trailing update
+// between them. A wider diagonal block is one launch whose tile tasks run concurrently, so
+// fewer, wider panels shorten the serial chain of blocks (B200: b1n4096 1.38 / 1.33 / 1.21 ms
+// at NB = 512 / 768 / 1024, b1n16384 12.56 / 12.19 / 12.21, b1n32768 81.5 / 76.9 / 77.0).
+// But the panel solve and the trailing update run K = NB through the 3xTF32 accumulator,
+// whose error grows with K: on spectral inputs of condition 1e5 the relative residual is
+// 5.0e-6 / 7.5e-6 / 1.0e-5 (n = 4096), against the 1e-5 gate. So NB = 768 above n = 2048
+// (the gate kept with a margin) and 512 up to n = 2048 (b8n2048: 0.83 ms against 0.85).
 int64_t outer_width(int64_t n) {
-  // n <= 1024: one outer panel (left-looking 64-wide steps); larger: 512-wide panels with
-  // a rank-512 trailing update between them.
   if (g_outer_width > 0 && g_outer_width % 64 == 0) return n <= g_outer_width ? n : g_outer_width;
-  return n <= 1024 ? n : 512;
+  if (n <= 1024) return n;
+  return n <= 2048 ? 512 : 768;
 }
 
 struct DeviceState {

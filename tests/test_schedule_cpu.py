@@ -32,8 +32,10 @@ ROOT = Path(__file__).resolve().parents[1]
     (3, 200, 11),           # chain with a ragged last block: 1 + 4 + 3 + 3
     (1, 2048, 16),          # 3 x (block, solve, split, trailing) + last block + copy,
                             # + 2 look-ahead splits (automatic for n <= 8192)
-    (1, 2100, 21),          # 4 full panels + a 52-wide last panel (one factor) + copy + 3 splits
-    (1, 16384, 126),        # 31 x 4 + last block + copy
+    (1, 2100, 35),          # 768-wide panels: 2 full ones (block, solve, split, trailing; one
+                            # look-ahead split) + a 564-wide last panel as a 64-wide chain
+                            # (9 factors, 8 updates, 8 solves) + copy
+    (1, 16384, 86),         # 768-wide panels: 21 x 4 + a 256-wide last block + copy
     (2, 1030, 50),          # rows not 16-byte multiples: the 64-wide steps in each panel
 ])
 def test_launch_counts_follow_the_schedule(batch, n, launches):
@@ -47,10 +49,10 @@ def test_lookahead_option():
         assert lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 0) == _lib.CHOL_OK
         assert int(lib.chol_launch_count(1, 2048)) == 14
         assert lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, 1) == _lib.CHOL_OK
-        assert int(lib.chol_launch_count(1, 16384)) > 126
+        assert int(lib.chol_launch_count(1, 16384)) > 86
     finally:
         lib.chol_set_option(_lib.CHOL_OPT_LOOKAHEAD, -1)
-    assert int(lib.chol_launch_count(1, 16384)) == 126   # automatic: off above n = 8192
+    assert int(lib.chol_launch_count(1, 16384)) == 86    # automatic: off above n = 8192
 
 
 def test_chain_width_option():

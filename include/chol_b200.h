@@ -273,10 +273,10 @@ CHOL_API int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w
    of C (and row c of Q) stands for global column c + (c / col_block) * (col_stride -
    col_block), and lower_only compares that global column with the row. One launch updates
    every trailing block a rank owns. col_block must be 256 and col_stride a multiple of it
-   (tensor-core path; needs 16-byte aligned rows). With P == Q (the driver's case) the TF32
-   low parts of P are computed once into a scratch buffer the library caches per device
-   (grown with cudaMalloc on first need; calls that overlap on the GPU race on it) and
-   loaded by the GEMM instead of split in shared memory. */
+   (tensor-core path; needs 16-byte aligned rows). With P == Q (the driver's case) and more
+   than one column block, the TF32 low parts of P are computed once into a scratch buffer
+   the library caches per device (grown with cudaMalloc on first need; calls that overlap
+   on the GPU race on it) and loaded by the GEMM instead of split in shared memory. */
 CHOL_API int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t ncols, int64_t K,
                                      const float* P, int64_t ldp, const float* Q, int64_t ldq,
                                      float alpha, float beta, int64_t diag_offset, int lower_only,

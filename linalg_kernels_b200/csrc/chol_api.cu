@@ -1006,9 +1006,12 @@ int chol_gemm_nt_cyclic_f32(float* C, int64_t ldc, int64_t m, int64_t ncols, int
   g.cmap_stride = col_stride;
   if (!tc_supported(g)) return CHOL_ERR_UNSUPPORTED;
   cudaStream_t q = static_cast<cudaStream_t>(queue);
-  if (P == Q && ldp == ldq && K % 4 == 0 && g_gemm_engine != 1) {
-    // low TF32 parts of the panel once (cached scratch), then the GEMM loads them with TMA
-    // instead of splitting every tile in shared memory
+  // Several column blocks: each row tile of P feeds many output tiles, so its low TF32 parts
+  // are computed once (cached scratch) and loaded by TMA instead of split in shared memory
+  // for every tile. One block (the look-ahead update): each row tile is used once, and the
+  // separate pass costs more than it saves (m = 32512, K = 256: 13 + 53 us against 44 us
+  // for the in-kernel split).
+  if (P == Q && ldp == ldq && K % 4 == 0 && g_gemm_engine != 1 && ncols > col_block) {
     static PanelScratch lo_cache[64];
     float* lo = dev < 64 ? static_cast<float*>(cached_scratch(lo_cache[dev],
                                                               size_t(m) * size_t(K) * 4))

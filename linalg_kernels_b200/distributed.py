@@ -347,10 +347,13 @@ def factor_batch_sharded(a: torch.Tensor | None, batch: int, n: int, pg, factor=
         if a is None or tuple(a.shape) != (batch, n, n) or not a.is_contiguous():
             raise ValueError("the root needs the contiguous (batch, n, n) input")
         sends = [pg.P2POp(pg.isend, a[o:o + c], r) for r, (o, c) in enumerate(sl) if r != root]
-        for w in _p2p(pg, sends):
-            w.wait()
+        sent = _p2p(pg, sends)
+        # the root's own slice is disjoint from what it sends: it is factored while the
+        # sends are in flight (NCCL runs them on its own queue)
         mine = a[off:off + cnt]
         l_mine = factor(mine)
+        for w in sent:
+            w.wait()
         out = torch.empty(batch, n, n, dtype=a.dtype, device=a.device)
         recvs = [pg.P2POp(pg.irecv, out[o:o + c], r) for r, (o, c) in enumerate(sl)
                  if r != root]

@@ -11,22 +11,26 @@
 //             so that a column read by 32 consecutive rows hits 32 distinct banks; warp w
 //             copies rows w, w + 8, ... (coalesced).
 //   per panel k0 = 0, 32, ...:
-//     factor  warp 0, lane i holding row k0 + i of the 32 x 32 diagonal block in
-//             registers: per column j the pivot comes from lane j by shuffle, r = rsqrt(d),
-//             L[j][j] = d r and L[i][j] = a[i][j] r below it (the pivot arithmetic of the
-//             small kernel), and the rank-1 update of the rest of the block takes each
-//             L[c][j] from lane c by shuffle. r is kept per column for the solve.
-//     solve   one thread per row below the block: x = a L_D^{-T} by forward substitution
-//             (x_j = (a_j - sum_{i<j} x_i L_D[j][i]) r_j) in chunks of 8 columns, the L_D
-//             entries read as shared-memory broadcasts.
+//     panel   the warps that hold rows k0..n-1 (one row per thread, its w <= 32 panel
+//             entries in registers) factor the whole n - k0 by w panel in one right-looking
+//             pass: per column j every thread scales its entry by r = rsqrt(d), where the
+//             pivot d comes from shared memory (the owner of row k0 + j prepared it in the
+//             previous column: look-ahead), the diagonal block's rows publish their entry
+//             of column j into a ping-pong buffer, one named barrier of the panel's warps,
+//             and each row takes the rank-1 update of its remaining entries from broadcast
+//             reads. The diagonal block's factor and the solve of the rows below it are
+//             the same pass, so no warp waits for one warp's factor (the first version
+//             factored the block in warp 0 and then solved one row per thread:
+//             58.3 us at b256n128).
 //     update  the lower triangle of the trailing rows and columns minus X X^T, K = 32,
 //             thread (tx, ty) of a 16 x 16 grid owning the rows ty + 16 i and columns
 //             tx + 16 c (conflict-free shared-memory reads).
 //   store     L row by row with zeros above the diagonal (coalesced); info = the first
 //             diagonal entry that is not > 0 (a non-positive pivot makes every later pivot
 //             NaN, so the first one is LAPACK's info).
-// Shared memory: n (n | 1) floats (66 KB at n = 128); 2 CTAs per SM (the register budget
-// of 128 per thread lets the factor keep its shuffles in flight). No workspace, no
+// Shared memory: n (n | 1) floats (66 KB at n = 128) plus the panel's column buffer and
+// pivots; 2 CTAs per SM (128 registers per thread hold a thread's 32 panel entries and the
+// update's 21 accumulators without spilling). No workspace, no
 // waits on other CTAs. A == L (in place) is allowed: a CTA reads its whole matrix before
 // it writes any of it.
 #include "chol_common.cuh"
@@ -44,65 +48,56 @@ __device__ __forceinline__ float mid_rsqrt(float x) {
   return y;
 }
 
-// Warp 0: factor the w x w diagonal block at (k0, k0) in place; rdg[k0 + j] = r_j.
-__device__ __forceinline__ void mid_factor_diag(float* As, int ld, int k0, int w, int lane,
-                                                float* rdg) {
+// The panel's warps (rows k0..n-1, one row per thread: thread t holds row k0 + t, columns
+// k0..k0+w-1, in registers): the w columns of the panel, right-looking. Per column j: every
+// thread reads the pivot d from shared memory (the owner of row k0 + j prepared it in the
+// previous column from its own registers: look-ahead) and scales its entry by r = rsqrt(d)
+// (the diagonal row gets d r = sqrt(d)); the diagonal block's rows below j publish their
+// entry of column j; one barrier of the panel's warps; then every row below j takes the
+// rank-1 update of its remaining columns, reading the published column as shared-memory
+// broadcasts. This factors the diagonal block and solves the rows below it in one pass, so
+// no warp waits for a single warp's factor. cb: 2 x 32 floats (ping-pong), db: 2 floats.
+__device__ __forceinline__ void mid_panel(float* As, int ld, int n, int k0, int w, int tid,
+                                          float* cb, float* db) {
+  const int rows = n - k0;
+  const int nthr = (rows + 31) & ~31;
+  if (tid >= nthr) return;
+  const bool own = tid < rows;
+  float* rp = As + (k0 + (own ? tid : 0)) * ld + k0;
   float a[32];
-  const bool own = lane < w;
-  float* row = As + (k0 + lane) * ld + k0;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) a[j] = (own && j <= lane) ? row[j] : 0.f;
+  for (int c = 0; c < 32; ++c) a[c] = (own && c < w) ? rp[c] : 0.f;
+  if (tid == 0) db[0] = a[0];
+  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     if (j < w) {
-      const float d = __shfl_sync(0xffffffffu, a[j], j);
+      const float d = db[j & 1];
       const float r = mid_rsqrt(d);
-      a[j] = lane == j ? d * r : (lane > j ? a[j] * r : a[j]);
-      if (lane == 0) rdg[k0 + j] = r;
+      const float l = a[j] * r;
+      a[j] = l;
+      float* cj = cb + (j & 1) * 32;
+      if (tid > j && tid < w) cj[tid] = l;
+      if (tid == j + 1 && j + 1 < w) db[(j + 1) & 1] = fmaf(-l, l, a[j + 1]);
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      if (tid > j) {
+        // entries j+1..w-1 of this row (for a row of the diagonal block only those <= tid
+        // matter; the others lie above the diagonal and are never read)
 #pragma unroll
-      for (int c = j + 1; c < 32; ++c) {
-        const float lc = __shfl_sync(0xffffffffu, a[j], c);
-        a[c] = c <= lane ? fmaf(-a[j], lc, a[c]) : a[c];
+        for (int q = (j + 1) >> 2; q < 8; ++q) {
+          const float4 v = *reinterpret_cast<const float4*>(cj + 4 * q);
+          if (4 * q + 0 > j) a[4 * q + 0] = fmaf(-l, v.x, a[4 * q + 0]);
+          if (4 * q + 1 > j) a[4 * q + 1] = fmaf(-l, v.y, a[4 * q + 1]);
+          if (4 * q + 2 > j) a[4 * q + 2] = fmaf(-l, v.z, a[4 * q + 2]);
+          if (4 * q + 3 > j) a[4 * q + 3] = fmaf(-l, v.w, a[4 * q + 3]);
+        }
       }
     }
   }
   if (own) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j <= lane) row[j] = a[j];
-  }
-}
-
-// One thread: row R of the panel, x = a L_D^{-T}, in chunks of 8 columns: a chunk first
-// takes the contributions of the columns already solved (read back from the row itself),
-// then solves its own 8 x 8 triangle in registers.
-__device__ __forceinline__ void mid_solve_row(float* As, int ld, int k0, int w, int R,
-                                              const float* rdg) {
-  float* row = As + R * ld + k0;
-  for (int q = 0; q < w; q += 8) {
-    float x[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) x[c] = (q + c < w) ? row[q + c] : 0.f;
-    const float* lq = As + (k0 + q) * ld + k0;  // L_D[q + c][i] at lq[c * ld + i]
-#pragma unroll 4
-    for (int i = 0; i < q; ++i) {
-      const float xi = row[i];
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        if (q + c < w) x[c] = fmaf(-xi, lq[c * ld + i], x[c]);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (q + j < w) {
-        x[j] *= rdg[k0 + q + j];
-#pragma unroll
-        for (int c = j + 1; c < 8; ++c)
-          if (q + c < w) x[c] = fmaf(-x[j], lq[c * ld + q + j], x[c]);
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-      if (q + c < w) row[q + c] = x[c];
+    for (int c = 0; c < 32; ++c)
+      if (c < w) rp[c] = a[c];
   }
 }
 
@@ -149,13 +144,17 @@ __device__ __forceinline__ void mid_update(float* As, int ld, int n, int k0, int
     }
 }
 
+// The panel's column buffer and pivots follow the matrix (offset in floats, 16-byte aligned).
+__host__ __device__ __forceinline__ int mid_aux_offset(int n) { return (n * (n | 1) + 3) & ~3; }
+
 __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
     mid_potrf_kernel(const float* A, float* L, int64_t batch, int n, int* info) {
   griddep_wait();
   griddep_launch();
   extern __shared__ float As[];
-  __shared__ float rdg[kMidMax];
   const int ld = n | 1;
+  float* cb = As + mid_aux_offset(n);  // 2 x 32 floats, 16-byte aligned
+  float* db = cb + 64;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int64_t m = blockIdx.x; m < batch; m += gridDim.x) {
     const float* Am = A + m * int64_t(n) * n;
@@ -166,12 +165,10 @@ __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
     __syncthreads();
     for (int k0 = 0; k0 < n; k0 += 32) {
       const int w = min(32, n - k0);
-      if (warp == 0) mid_factor_diag(As, ld, k0, w, lane, rdg);
+      mid_panel(As, ld, n, k0, w, tid, cb, db);
       __syncthreads();
       const int k1 = k0 + w;
       if (k1 < n) {
-        if (tid < n - k1) mid_solve_row(As, ld, k0, w, k1 + tid, rdg);
-        __syncthreads();
         mid_update(As, ld, n, k0, w, k1, tid);
         __syncthreads();
       }
@@ -192,7 +189,7 @@ __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
   }
 }
 
-size_t mid_smem_bytes(int n) { return size_t(n) * size_t(n | 1) * sizeof(float); }
+size_t mid_smem_bytes(int n) { return (size_t(mid_aux_offset(n)) + 72) * sizeof(float); }
 
 }  // namespace
 

@@ -178,6 +178,12 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   the chain's GEMMs take 128 columns at a time; it needs 64 KiB more workspace per matrix
  *   (chol_workspace_bytes includes it; a smaller workspace falls back to 64). */
 #define CHOL_OPT_CHAIN_WIDTH 10
+/*   CHOL_OPT_GEMM_CTAS: cap on the grid of every tensor-core GEMM launch that the CALLING
+ *   THREAD issues (0 = default: one CTA per SM; the only thread-local option). A caller that
+ *   feeds two queues of one device from one thread sets it before each queue's calls, so that
+ *   the two queues' persistent GEMMs hold disjoint shares of the SMs and neither waits for
+ *   the other to finish (the multi-GPU driver's panel chain and trailing update). */
+#define CHOL_OPT_GEMM_CTAS 11
 CHOL_API int chol_set_option(int option, int value);
 
 /*

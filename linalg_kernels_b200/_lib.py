@@ -35,6 +35,7 @@ CHOL_OPT_OVERLAP_CALLS = 7
 CHOL_OPT_MID_KERNEL = 8
 CHOL_OPT_WAIT_LIMIT_US = 9
 CHOL_OPT_CHAIN_WIDTH = 10
+CHOL_OPT_GEMM_CTAS = 11
 ENGINE_AUTO, ENGINE_FMA, ENGINE_TENSOR = 0, 1, 2
 
 _i64 = ctypes.c_int64

@@ -681,6 +681,9 @@ int prepare_kernels(int /*device*/) {
 uint64_t g_wait_limit_ns = 2000000000ull;
 uint64_t wait_limit_ns() { return g_wait_limit_ns; }
 
+thread_local int t_gemm_ctas = 0;
+int gemm_cta_cap() { return t_gemm_ctas; }
+
 int g_gemm_engine = 0;
 
 int launch_gemm(const GemmArgs& g, cudaStream_t q, bool pdl) {
@@ -806,6 +809,11 @@ int chol_set_option(int option, int value) {
   if (option == CHOL_OPT_CHAIN_WIDTH) {
     if (value != 64 && value != 128) return CHOL_ERR_INVALID_ARG;
     g_chain_width = value;
+    return CHOL_OK;
+  }
+  if (option == CHOL_OPT_GEMM_CTAS) {
+    if (value < 0 || value > 4096) return CHOL_ERR_INVALID_ARG;
+    t_gemm_ctas = value;
     return CHOL_OK;
   }
   if (option == CHOL_OPT_WAIT_LIMIT_US) {

@@ -233,6 +233,8 @@ cudaError_t prepare_tc();
 int read_and_clear_status(int* out);
 // Bound of the inter-CTA flag waits (CHOL_OPT_WAIT_LIMIT_US; 2 s by default).
 uint64_t wait_limit_ns();
+// Cap on tensor-core GEMM grids set by the calling thread (CHOL_OPT_GEMM_CTAS; 0 = none).
+int gemm_cta_cap();
 // One CTA waiting with the bounded flag wait for words[0] == value (words[1]: abort word).
 int launch_flag_wait(int* words, int value, cudaStream_t q);
 // Device address of the status word (for kernels in other translation units).

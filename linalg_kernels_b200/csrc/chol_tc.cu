@@ -473,6 +473,8 @@ int launch_tc_maps(const GemmArgs& g, const CUtensorMap& mp, const CUtensorMap& 
   }
   int64_t ctas = ts.total < sms ? ts.total : sms;
   if (max_ctas > 0 && ctas > max_ctas) ctas = max_ctas;
+  const int cap = gemm_cta_cap();
+  if (cap > 0 && ctas > cap) ctas = cap;
   if (mplo != nullptr && mqlo != nullptr)
     return status_from(launch_pdl(tc_gemm_kernel<BN, true>, dim3(unsigned(ctas)), dim3(kThreads),
                                   Cfg::SMEM, q, pdl, mp, mq, *mplo, *mqlo, g, ts, org, status));

@@ -16,18 +16,24 @@ row-major in a local ``(n, n_local)`` tensor. For every block column ``j``:
    block with ``chol_gemm_nt_cyclic_f32`` (the GEMM maps local column blocks to their
    global columns, so masking and Q's rows follow the cyclic layout).
 
-Look-ahead: the owner of block ``j+1`` first updates that block with panel ``j``, factors
-it and starts its broadcast; only then does every rank update its remaining blocks, so the
-broadcast of panel ``j+1`` overlaps the bulk of step ``j``'s update.
+Look-ahead of depth 2 on two queues of each GPU: when panel ``j`` has arrived, the
+high-priority "chain" queue updates blocks ``j+1`` and ``j+2`` with it (on their owners),
+and the owner of ``j+1`` factors it and starts its broadcast; the low-priority "bulk" queue
+updates every block right of ``j+2``. A block leaves the bulk set one step before the chain
+needs it, so each bulk update has two chain steps to finish in, and the chain never waits
+behind a bulk update in queue order. Events order the two queues (the chain's update of
+block ``j+2`` waits for the bulk's previous work, the bulk waits for panel ``j``, a receive
+buffer is rewritten only after the bulk has read it). Both queues' GEMMs run with capped
+grids (``CHOL_OPT_GEMM_CTAS``), so that the persistent kernels of one queue never hold SMs
+the other needs, and some SMs stay free for NCCL.
 
-Paired updates: the update of the blocks right of the look-ahead block is deferred every
-other step and then applied for two panels at once, ``P = [panel j-1 | panel j]`` (K = 2 bs
-= 512), copied side by side into one buffer. A K = 256 update spends as long in its
-epilogue (the read-modify-write of C) as in its tensor-core main loop; at K = 512 the main
-loop hides it, and the trailing matrix is read and written half as often. The look-ahead
-block still receives every panel before it is factored. Receive buffers rotate over three
-panels (the deferred one, the current one and the one in flight). Every rank issues the
-same collectives in the same order.
+Paired updates: the bulk update is deferred every other step and then applied for two
+panels at once, ``P = [panel j-1 | panel j]`` (K = 2 bs = 512), copied side by side into one
+buffer (by the bulk queue; the chain's update of block ``j+2`` takes the same K = 512
+product). A K = 256 update spends as long in its epilogue (the read-modify-write of C) as
+in its tensor-core main loop; at K = 512 the main loop hides it, and the trailing matrix is
+read and written half as often. Receive buffers rotate over four panels. Every rank issues
+the same collectives in the same order.
 
 The arithmetic goes through an ``ops`` object: ``CudaOps`` (the C ABI of libchol_b200.so,
 the product path). Tests substitute a CPU implementation to check the schedule with
@@ -36,6 +42,7 @@ the product path). Tests substitute a CPU implementation to check the schedule w
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from dataclasses import dataclass
 
@@ -113,6 +120,9 @@ class CudaOps:
 
     def _q(self):
         return ctypes.c_void_p(_lib.current_queue(self.device))
+
+    def queues(self, chain_ctas: int, bulk_ctas: int) -> "QueuePair":
+        return QueuePair(self, chain_ctas, bulk_ctas)
 
     def potrf_block(self, diag: torch.Tensor, tinv: torch.Tensor, info: torch.Tensor | None):
         """Factor diag (kb x kb view, kb <= 64) in place; tinv (64 x 64) <- inv(L)."""
@@ -213,37 +223,124 @@ def _update_blocks(local: torch.Tensor, lay: CyclicLayout, blocks: list[int], fi
     ops.cyclic_update(local[c0:, lc0:lc0 + width], p, bs, bs * lay.world)
 
 
+class _OneQueue:
+    """Stand-in for a queue pair where ops has none (CPU ops): one queue, no events."""
+
+    def on(self, name):
+        return contextlib.nullcontext()
+
+    def record(self):
+        return None
+
+    def wait(self, ev):
+        pass
+
+    def join(self):
+        pass
+
+
+class QueuePair:
+    """Two torch queues of one device for the column-cyclic schedule: "chain" (high priority:
+    the look-ahead updates, the panel factor and its broadcast) and "bulk" (low priority: the
+    update of every block right of the look-ahead blocks), each with its own cap on the
+    library's tensor-core GEMM grids (``CHOL_OPT_GEMM_CTAS``, set per call from this thread)
+    so that the persistent GEMMs of the two queues hold disjoint SMs and leave some free for
+    NCCL. Both queues start after the caller's queue and the caller's queue waits for both
+    at ``join``."""
+
+    def __init__(self, ops: "CudaOps", chain_ctas: int, bulk_ctas: int):
+        self.ops = ops
+        dev = ops.device
+        self.caller = torch.cuda.current_stream(dev)
+        self.streams = {"chain": torch.cuda.Stream(dev, priority=-1),
+                        "bulk": torch.cuda.Stream(dev, priority=0)}
+        self.caps = {"chain": int(chain_ctas), "bulk": int(bulk_ctas)}
+        start = self.caller.record_event()
+        for q in self.streams.values():
+            q.wait_event(start)
+
+    @contextlib.contextmanager
+    def on(self, name):
+        with torch.cuda.stream(self.streams[name]):
+            _lib.check(self.ops.lib.chol_set_option(_lib.CHOL_OPT_GEMM_CTAS, self.caps[name]),
+                       "chol_set_option")
+            try:
+                yield
+            finally:
+                self.ops.lib.chol_set_option(_lib.CHOL_OPT_GEMM_CTAS, 0)
+
+    def record(self):
+        return torch.cuda.current_stream(self.ops.device).record_event()
+
+    def wait(self, ev):
+        if ev is not None:
+            torch.cuda.current_stream(self.ops.device).wait_event(ev)
+
+    def join(self):
+        for q in self.streams.values():
+            self.caller.wait_stream(q)
+
+
+# (chain, bulk) GEMM CTA caps of the two queues over several ranks; 148 - 132 = 16 SMs stay
+# free for NCCL's kernels. At 2 GPUs, n = 32768: 54.7 ms in order, 51.3 ms at (40, 92),
+# 51.9 at (32, 100), 52.1 at (48, 84), 56.2 at (24, 108), 60.4 at (64, 64), 54.0 uncapped.
+AUTO_QUEUES = (40, 92)
+
+
 def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=None, ops=None,
-                        info: torch.Tensor | None = None, paired: bool = True) -> torch.Tensor:
+                        info: torch.Tensor | None = None, paired: bool = True,
+                        queues: tuple[int, int] | None | str = "auto") -> torch.Tensor:
     """Factor in place the block-column-cyclic matrix whose local columns are ``local``.
 
     ``pg`` is ``torch.distributed`` (or None for a single rank); ``ops`` defaults to
-    ``CudaOps`` on ``local``'s device. ``paired`` defers every other update of the blocks
-    right of the look-ahead block and applies two panels at once (K = 2 bs). Returns
-    ``local`` (now this rank's columns of L).
+    ``CudaOps`` on ``local``'s device. Look-ahead of depth 2: at step ``j`` (panel ``j``
+    received) the chain queue updates blocks ``j+1`` and ``j+2`` with it and factors and
+    broadcasts block ``j+1``; the bulk queue updates the blocks right of ``j+2``. A block
+    leaves the bulk set one step before the chain needs it, so each bulk update has two
+    steps of the chain to finish in. ``paired`` defers every other bulk update and applies
+    two panels at once (K = 2 bs). ``queues`` = (chain, bulk) GEMM CTA caps of the two
+    queues (``QueuePair``); None runs everything in order on the caller's queue; "auto" =
+    ``AUTO_QUEUES`` over several ranks and None on one (there the bulk is the whole
+    trailing update and every SM it gives up costs more than the overlap wins: n = 32768
+    on one GPU 86.1 ms in order, 90.0 ms at (32, 100)). Returns ``local`` (now this rank's
+    columns of L).
     """
+    if isinstance(queues, str):
+        if queues != "auto":
+            raise ValueError(f"queues: {queues!r}")
+        queues = AUTO_QUEUES if lay.world > 1 else None
     if ops is None:
         ops = CudaOps(local.device)
     n, bs = lay.n, lay.bs
     nb = lay.nblocks
     dev = local.device
     tinv = torch.zeros(64, 64, dtype=local.dtype, device=dev)
-    paired = paired and nb > 2
-    bufs = [torch.empty(n * bs, dtype=local.dtype, device=dev) for _ in range(3 if paired else 2)]
-    comb = torch.empty(n * 2 * bs, dtype=local.dtype, device=dev) if paired else None
+    paired = paired and nb > 3
+    nbuf = 4  # panel j's buffer is rewritten by panel j + 4 (its readers end at step j + 1)
+    bufs = [torch.empty(n * bs, dtype=local.dtype, device=dev) for _ in range(nbuf)]
+    combs = [torch.empty(n * 2 * bs, dtype=local.dtype, device=dev) for _ in range(2 if paired else 0)]
+    make = getattr(ops, "queues", None)
+    qs = make(*queues) if (queues is not None and make is not None) else _OneQueue()
+    owned = lay.owned()
+
+    def mine(t):
+        return t < nb and lay.owner(t) == lay.rank
 
     def panel_view(j):
         rows = n - j * bs
-        return bufs[j % len(bufs)][: rows * lay.width(j)].view(rows, lay.width(j))
+        return bufs[j % nbuf][: rows * lay.width(j)].view(rows, lay.width(j))
 
-    def factor_and_publish(j):
-        """The owner factors block j (fully updated) into the send buffer; every rank joins
-        the broadcast. The owner copies the solved rows back into its own columns after the
-        broadcast is issued, so that copy runs beside the send instead of before it. Returns
-        the work handle."""
+    bulk_done = {}  # step -> event after the bulk queue's work of that step
+
+    def publish(j):
+        """Chain queue: the owner factors block j (fully updated) into its send buffer; every
+        rank joins the broadcast. The owner copies the solved rows back into its own columns
+        after the broadcast is issued, so that copy runs beside the send. Returns the work
+        handle."""
+        qs.wait(bulk_done.get(j - nbuf + 1))  # the buffer's previous panel is read out
         pv = panel_view(j)
         back = None
-        if lay.owner(j) == lay.rank:
+        if mine(j):
             back = _factor_panel(local, lay, j, ops, tinv, info, out=pv, defer_copy=True)
         handle = None
         if pg is not None and lay.world > 1:
@@ -253,46 +350,48 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
             back[0].copy_(back[1])
         return handle
 
-    def combined(p, j, r0):
-        """[panel p | panel j] over the global rows r0..n, side by side in one buffer."""
-        rows = n - r0
-        pw = comb[: rows * 2 * bs].view(rows, 2 * bs)
-        pw[:, :bs].copy_(panel_view(p)[r0 - p * bs:])
-        pw[:, bs:].copy_(panel_view(j)[r0 - j * bs:])
-        return pw
-
-    work = factor_and_publish(0)
-    pending = None  # panel whose update of the blocks right of the look-ahead is deferred
+    with qs.on("chain"):
+        work = publish(0)
+    pending = None  # step whose bulk update is deferred to the next step (paired)
+    ncomb = 0  # combined buffers alternate: one is read while the next is written
     for j in range(nb):
-        if work is not None:
-            work.wait()
-        nxt = j + 1
-        work = None
-        rest = [t for t in lay.owned() if t > nxt]
-        owns_next = nxt < nb and lay.owner(nxt) == lay.rank
-        pw = None
-        if pending is not None and (rest or owns_next):
-            # P = [panel pending | panel j] from the look-ahead block's first row down: one
-            # K = 2 bs update for the look-ahead block and one for the blocks right of it
-            pw = combined(pending, j, nxt * bs)
-        if nxt < nb:
-            if owns_next:
-                if pw is not None:
-                    _update_blocks(local, lay, [nxt], nxt * bs, pw, ops)
+        l1, l2 = j + 1, j + 2
+        with qs.on("chain"):
+            if work is not None:
+                work.wait()
+            ready = qs.record()
+        rest = [t for t in owned if t > l2]
+        defer = paired and pending is None and l2 + 1 < nb
+        comb = None
+        with qs.on("bulk"):
+            qs.wait(ready)
+            if pending is not None and (rest or mine(l2)):
+                # P = [panel pending | panel j] from block l2's first row down, side by side
+                rows = n - l2 * bs
+                comb = combs[ncomb % 2][: rows * 2 * bs].view(rows, 2 * bs)
+                ncomb += 1
+                comb[:, :bs].copy_(panel_view(pending)[l2 * bs - pending * bs:])
+                comb[:, bs:].copy_(panel_view(j)[l2 * bs - j * bs:])
+            pre = qs.record()  # the bulk's earlier updates and this step's P are in place
+            if rest and not defer:
+                if comb is not None:
+                    _update_blocks(local, lay, rest, l2 * bs, comb, ops)
                 else:
-                    _update_blocks(local, lay, [nxt], j * bs, panel_view(j), ops)
-            work = factor_and_publish(nxt)
-        if not rest:
-            pending = None
-            continue
-        if paired and pending is None and nxt + 1 < nb:
-            pending = j  # applied together with panel j + 1 at the next step
-            continue
-        if pw is None:
-            _update_blocks(local, lay, rest, j * bs, panel_view(j), ops)
-        else:
-            _update_blocks(local, lay, rest, nxt * bs, pw, ops)
-        pending = None
+                    _update_blocks(local, lay, rest, j * bs, panel_view(j), ops)
+            bulk_done[j] = qs.record()
+        with qs.on("chain"):
+            if mine(l1):
+                _update_blocks(local, lay, [l1], j * bs, panel_view(j), ops)
+            work = publish(l1) if l1 < nb else None
+            if mine(l2):
+                qs.wait(pre)  # block l2 left the bulk set at this step
+                if comb is not None:
+                    _update_blocks(local, lay, [l2], l2 * bs, comb, ops)
+                else:
+                    _update_blocks(local, lay, [l2], j * bs, panel_view(j), ops)
+        bulk_done.pop(j - nbuf, None)
+        pending = j if defer else None
+    qs.join()
     return local
 
 

@@ -29,6 +29,29 @@ def test_cyclic_single_rank_matches_oracle(n, bs):
     assert res["ok"], res
 
 
+@pytest.mark.parametrize("queues", [(32, 100), (148, 148), (8, 8)])
+@pytest.mark.parametrize("paired", [True, False])
+def test_cyclic_queue_pair_matches_one_queue(queues, paired):
+    """The chain/bulk queue pair (any GEMM CTA caps) computes bitwise what the same schedule
+    computes in order on one queue: the events order every block's updates the same way, and a
+    cap changes which CTA computes a tile, not its arithmetic."""
+    from linalg_kernels_b200 import _lib
+
+    n, bs = 2560, 256
+    a, cond = inputs.covariance(1, n, 0.5, 4100)
+    lay = CyclicLayout(n, 1, 0, bs)
+    base = scatter_block_cyclic(a[0].to(DEV), lay)
+    one = factor_block_cyclic(base.clone(), lay, pg=None, paired=paired, queues=None)
+    two = factor_block_cyclic(base.clone(), lay, pg=None, paired=paired, queues=queues)
+    torch.cuda.synchronize()
+    assert torch.equal(one, two)
+    lib = _lib.load()
+    assert lib.chol_set_option(_lib.CHOL_OPT_GEMM_CTAS, -1) == _lib.CHOL_ERR_INVALID_ARG
+    l = gather_block_cyclic([two], n, 1, bs).cpu().numpy()[None]
+    l_or, _ = oracle.potrf(a.numpy())
+    assert oracle.check_factor(a.numpy(), l, l_ref=l_or, cond=cond.numpy())["ok"]
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_cyclic_emulated_ranks_on_one_gpu(world):
     """Each emulated rank's columns factored by the same schedule must equal the

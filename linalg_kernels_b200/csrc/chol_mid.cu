@@ -64,84 +64,119 @@ __device__ __forceinline__ void mid_panel(float* As, int ld, int n, int k0, int 
   if (tid >= nthr) return;
   const bool own = tid < rows;
   float* rp = As + (k0 + (own ? tid : 0)) * ld + k0;
-  float a[32];
+  // a[p] = entries (2p, 2p+1) of this thread's row, for the packed FMA
+  uint64_t a[16];
 #pragma unroll
-  for (int c = 0; c < 32; ++c) a[c] = (own && c < w) ? rp[c] : 0.f;
-  if (tid == 0) db[0] = a[0];
+  for (int p = 0; p < 16; ++p)
+    a[p] = pack2((own && 2 * p < w) ? rp[2 * p] : 0.f, (own && 2 * p + 1 < w) ? rp[2 * p + 1] : 0.f);
+  if (tid == 0) db[0] = lo_of(a[0]);
   asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     if (j < w) {
       const float d = db[j & 1];
       const float r = mid_rsqrt(d);
-      const float l = a[j] * r;
-      a[j] = l;
+      const uint64_t cur = a[j >> 1];
+      const float l = ((j & 1) ? hi_of(cur) : lo_of(cur)) * r;
+      a[j >> 1] = (j & 1) ? pack2(lo_of(cur), l) : pack2(l, hi_of(cur));
       float* cj = cb + (j & 1) * 32;
       if (tid > j && tid < w) cj[tid] = l;
-      if (tid == j + 1 && j + 1 < w) db[(j + 1) & 1] = fmaf(-l, l, a[j + 1]);
+      if (tid == j + 1 && j + 1 < w) {
+        const uint64_t nx = a[(j + 1) >> 1];
+        db[(j + 1) & 1] = fmaf(-l, l, ((j + 1) & 1) ? hi_of(nx) : lo_of(nx));
+      }
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      if (tid > j) {
-        // entries j+1..w-1 of this row (for a row of the diagonal block only those <= tid
+      if (tid > j && j + 1 < 32) {
+        // entries j+1..31 of this row (for a row of the diagonal block only those <= tid
         // matter; the others lie above the diagonal and are never read)
+        const float nl = -l;
+        int p0 = (j + 1) >> 1;
+        if ((j + 1) & 1) {  // odd first entry: the high half alone, then whole pairs
+          const uint64_t v = a[p0];
+          a[p0] = pack2(lo_of(v), fmaf(nl, cj[j + 1], hi_of(v)));
+          ++p0;
+        }
+        const uint64_t nl2 = pack2(nl, nl);
 #pragma unroll
-        for (int q = (j + 1) >> 2; q < 8; ++q) {
-          const float4 v = *reinterpret_cast<const float4*>(cj + 4 * q);
-          if (4 * q + 0 > j) a[4 * q + 0] = fmaf(-l, v.x, a[4 * q + 0]);
-          if (4 * q + 1 > j) a[4 * q + 1] = fmaf(-l, v.y, a[4 * q + 1]);
-          if (4 * q + 2 > j) a[4 * q + 2] = fmaf(-l, v.z, a[4 * q + 2]);
-          if (4 * q + 3 > j) a[4 * q + 3] = fmaf(-l, v.w, a[4 * q + 3]);
+        for (int q = p0 >> 1; q < 8; ++q) {
+          const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(cj + 4 * q);
+          if (2 * q >= p0) a[2 * q] = ffma2_u64(nl2, v.x, a[2 * q]);
+          a[2 * q + 1] = ffma2_u64(nl2, v.y, a[2 * q + 1]);
         }
       }
     }
   }
   if (own) {
 #pragma unroll
-    for (int c = 0; c < 32; ++c)
-      if (c < w) rp[c] = a[c];
+    for (int p = 0; p < 16; ++p) {
+      if (2 * p < w) rp[2 * p] = lo_of(a[p]);
+      if (2 * p + 1 < w) rp[2 * p + 1] = hi_of(a[p]);
+    }
   }
 }
 
 // All threads: the lower triangle of rows / columns [k1, n) minus X X^T, where X is
 // columns [k0, k0 + w) of those rows. Thread (tx, ty) owns rows k1 + ty + 16 i and columns
-// k1 + tx + 16 c with c <= i < 6 (for c > i every entry lies above the diagonal): per k a
-// warp reads 2 rows (broadcasts) and 16 consecutive rows n | 1 floats apart (distinct
-// banks), so the reads are conflict-free.
-__device__ __forceinline__ void mid_update(float* As, int ld, int n, int k0, int w, int k1,
-                                           int tid) {
+// k1 + tx + 16 c with c <= i < T, T = the trailing rows' 16-row tiles (<= 6, a compile-time
+// count so that no work or select is spent on absent tiles; for c > i every entry lies
+// above the diagonal): per k a warp reads 2 rows (broadcasts) and 16 consecutive rows
+// n | 1 floats apart (distinct banks), so the reads are conflict-free. Rows are paired for
+// the packed FMA.
+template <int T>
+__device__ __forceinline__ void mid_update_t(float* As, int ld, int n, int k0, int w, int k1,
+                                             int tid) {
+  constexpr int P = (T + 1) / 2;  // row pairs
   const int tx = tid & 15, ty = tid >> 4;
-  const int tiles = (n - k1 + 15) >> 4;  // <= 6
-  int ro[6], co[6];
+  int ro[2 * P], co[T];
 #pragma unroll
-  for (int i = 0; i < 6; ++i) {
-    // rows past n read row n - 1 (in bounds); their results are not written
+  for (int i = 0; i < 2 * P; ++i)  // rows past n read row n - 1 (in bounds); not written
     ro[i] = min(k1 + ty + 16 * i, n - 1) * ld + k0;
-    co[i] = min(k1 + tx + 16 * i, n - 1) * ld + k0;
-  }
-  float acc[6][6];
 #pragma unroll
-  for (int i = 0; i < 6; ++i)
+  for (int c = 0; c < T; ++c) co[c] = min(k1 + tx + 16 * c, n - 1) * ld + k0;
+  // acc[p][c] = (rows 2p, 2p+1) x column c, packed for fma.rn.f32x2; c <= 2p + 1
+  uint64_t acc[P][T];
 #pragma unroll
-    for (int c = 0; c <= i; ++c) acc[i][c] = 0.f;
+  for (int p = 0; p < P; ++p)
+#pragma unroll
+    for (int c = 0; c < T; ++c) acc[p][c] = 0ull;
 #pragma unroll 4
   for (int j = 0; j < w; ++j) {
-    float xr[6], xc[6];
+    uint64_t xr[P];
+    float xc[T];
 #pragma unroll
-    for (int i = 0; i < 6; ++i) {
-      xr[i] = i < tiles ? As[ro[i] + j] : 0.f;
-      xc[i] = i < tiles ? As[co[i] + j] : 0.f;
-    }
+    for (int p = 0; p < P; ++p) xr[p] = pack2(As[ro[2 * p] + j], As[ro[2 * p + 1] + j]);
 #pragma unroll
-    for (int i = 0; i < 6; ++i)
+    for (int c = 0; c < T; ++c) xc[c] = As[co[c] + j];
 #pragma unroll
-      for (int c = 0; c <= i; ++c) acc[i][c] = fmaf(xr[i], xc[c], acc[i][c]);
+    for (int p = 0; p < P; ++p)
+#pragma unroll
+      for (int c = 0; c < T; ++c)
+        if (c <= 2 * p + 1) acc[p][c] = ffma2_u64(xr[p], pack2(xc[c], xc[c]), acc[p][c]);
   }
 #pragma unroll
-  for (int i = 0; i < 6; ++i)
+  for (int p = 0; p < P; ++p)
 #pragma unroll
-    for (int c = 0; c <= i; ++c) {
-      const int r = k1 + ty + 16 * i, col = k1 + tx + 16 * c;
-      if (i < tiles && r < n && col <= r) As[r * ld + col] -= acc[i][c];
-    }
+    for (int c = 0; c < T; ++c)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = 2 * p + h;
+        const int r = k1 + ty + 16 * i, col = k1 + tx + 16 * c;
+        if (c <= 2 * p + 1 && i < T && r < n && col <= r)
+          As[r * ld + col] -= h ? hi_of(acc[p][c]) : lo_of(acc[p][c]);
+      }
+}
+
+// All threads, one instantiation per count of 16-row tiles of the trailing matrix.
+__device__ __forceinline__ void mid_update(float* As, int ld, int n, int k0, int w, int k1,
+                                           int tid) {
+  switch ((n - k1 + 15) >> 4) {
+    case 1: mid_update_t<1>(As, ld, n, k0, w, k1, tid); break;
+    case 2: mid_update_t<2>(As, ld, n, k0, w, k1, tid); break;
+    case 3: mid_update_t<3>(As, ld, n, k0, w, k1, tid); break;
+    case 4: mid_update_t<4>(As, ld, n, k0, w, k1, tid); break;
+    case 5: mid_update_t<5>(As, ld, n, k0, w, k1, tid); break;
+    default: mid_update_t<6>(As, ld, n, k0, w, k1, tid); break;
+  }
 }
 
 // The panel's column buffer and pivots follow the matrix (offset in floats, 16-byte aligned).

@@ -71,7 +71,8 @@ CHOL_API int chol_prepare(int device);
 
 /*
  * Bytes of device workspace chol_potrf_batched_ws_f32 needs for (batch, n).
- * 0 when the chosen kernels need none (n <= 128 with the default options).
+ * 0 when the chosen kernels need none (n <= 128, and 128 < n <= 256 where the one-CTA-per-
+ * matrix kernel takes it, with the default options: see CHOL_OPT_MID_KERNEL).
  */
 CHOL_API size_t chol_workspace_bytes(int64_t batch, int64_t n);
 
@@ -109,10 +110,11 @@ CHOL_API int chol_potrf_batched_ws_f32(const float* A, float* L, int64_t batch, 
  * cudaMalloc (a host that owns all device memory through its own pool, or a path where
  * cudaMalloc's implicit device synchronisation is not allowed): the caller passes A, L
  * and info as usual, and the scratch comes from a fixed 4 MiB device array inside the
- * library, held on every GPU that loads the library until exit. A call needs 16 KiB per
- * matrix with n > 128 (the 64 x 64 inverse diagonal blocks of the blocked path), so at most
- * 256 such matrices per call; larger batches return
- * CHOL_ERR_SCRATCH_LIMIT. n <= 128 needs none (with the default options). The optional
+ * library, held on every GPU that loads the library until exit. A call on the blocked path
+ * (n > 128, except the sizes CHOL_OPT_MID_KERNEL gives the one-CTA-per-matrix kernel) needs
+ * 16 KiB per matrix (the 64 x 64 inverse diagonal blocks), so at most 256 such matrices per
+ * call; larger batches return CHOL_ERR_SCRATCH_LIMIT. n <= 128 needs none (with the default
+ * options). The optional
  * regions of the blocked schedule are taken from the array when they fit after that.
  * The first call on a device looks up the array's device address with that device
  * current; make that first call before any stream capture. All calls share the array:
@@ -163,8 +165,10 @@ CHOL_API int64_t chol_launch_count(int64_t batch, int64_t n);
  *   work on its queue before reading. */
 #define CHOL_OPT_OVERLAP_CALLS 7
 /*   CHOL_OPT_MID_KERNEL: 1 (default) = 64 < n <= 128 is factored by one launch with one CTA
- *   per matrix held in shared memory, needing no workspace; 0 = the blocked schedule (the
- *   workspace sizes then follow it: size workspaces after setting this). */
+ *   per matrix held in shared memory, and 128 < n <= 256 with n % 64 != 0 (batch <= 296, or
+ *   n < 144) by one launch with one 512-thread CTA per matrix, both needing no workspace;
+ *   0 = the blocked schedule (the workspace sizes then follow it: size workspaces after
+ *   setting this). */
 #define CHOL_OPT_MID_KERNEL 8
 /*   CHOL_OPT_WAIT_LIMIT_US: bound, in microseconds, of the waits in which one CTA waits for
  *   a tile another CTA publishes (the diagonal-block kernel); 0 = the default, 2 s. A wait

@@ -97,7 +97,7 @@ bool overlaps_partially(const float* a, const float* b, int64_t count) {
 // the trailing GEMM loads instead of splitting in shared memory, and V = inv(L11) of the
 // panel's NB x NB diagonal block (NB x NB floats per matrix).
 size_t blocked_workspace_min(int64_t batch, int64_t n) {
-  if (n <= 64 || use_mid(n)) return 0;
+  if (n <= 64 || use_mid(batch, n)) return 0;
   return size_t(batch) * kBlock * kBlock * sizeof(float);
 }
 size_t blocked_lo_bytes(int64_t batch, int64_t n) {
@@ -146,7 +146,7 @@ size_t blocked_t128_bytes(int64_t batch, int64_t n) {
   return size_t(batch) * 128 * 128 * sizeof(float);
 }
 size_t blocked_workspace(int64_t batch, int64_t n) {
-  if (use_mid(n)) return 0;
+  if (use_mid(batch, n)) return 0;
   return blocked_workspace_min(batch, n) + blocked_lo_bytes(batch, n) +
          blocked_inv_bytes(batch, n) + blocked_diag_bytes(batch, n) +
          blocked_t128_bytes(batch, n);
@@ -580,7 +580,7 @@ int check_common(const float* A, float* L, int64_t batch, int64_t n) {
 int potrf_impl(const float* A, float* L, int64_t batch, int64_t n, int* info, void* ws,
                size_t ws_bytes, cudaStream_t q) {
   if (n <= 64) return launch_small(A, L, batch, int(n), info, q);
-  if (use_mid(n)) return launch_mid(A, L, batch, int(n), info, q);
+  if (use_mid(batch, n)) return launch_mid(A, L, batch, int(n), info, q);
   if (ws == nullptr || ws_bytes < blocked_workspace_min(batch, n)) return CHOL_ERR_WORKSPACE;
   if (batch > 0x7fffffffLL) return CHOL_ERR_UNSUPPORTED;
   return run_blocked(A, L, batch, n, info, static_cast<float*>(ws), ws_bytes, q);
@@ -766,7 +766,7 @@ int chol_potrf_batched_f32(const float* A, float* L, int64_t batch, int64_t n, i
 
 int64_t chol_launch_count(int64_t batch, int64_t n) {
   if (batch <= 0 || n <= 0) return 0;
-  if (n <= 64 || use_mid(n)) return 1;
+  if (n <= 64 || use_mid(batch, n)) return 1;
   return blocked_launches(batch, n);
 }
 

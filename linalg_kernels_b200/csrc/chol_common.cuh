@@ -162,7 +162,7 @@ int launch_small(const float* A, float* L, int64_t batch, int n, int* info, cuda
 // 64 < n <= 128: one CTA per matrix in shared memory (chol_mid.cu), unless
 // CHOL_OPT_MID_KERNEL is 0.
 extern int g_mid_kernel;
-bool use_mid(int64_t n);
+bool use_mid(int64_t batch, int64_t n);
 cudaError_t prepare_mid();
 int launch_mid(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q);
 // Overlap of back-to-back independent small calls on one queue (on by default).

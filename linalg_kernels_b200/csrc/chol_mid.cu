@@ -56,19 +56,10 @@ __device__ __forceinline__ float mid_rsqrt(float x) {
 // entry of column j; one barrier of the panel's warps; then every row below j takes the
 // rank-1 update of its remaining columns, reading the published column as shared-memory
 // broadcasts. This factors the diagonal block and solves the rows below it in one pass, so
-// no warp waits for a single warp's factor. cb: 2 x 32 floats (ping-pong), db: 2 floats.
-__device__ __forceinline__ void mid_panel(float* As, int ld, int n, int k0, int w, int tid,
-                                          float* cb, float* db) {
-  const int rows = n - k0;
-  const int nthr = (rows + 31) & ~31;
-  if (tid >= nthr) return;
-  const bool own = tid < rows;
-  float* rp = As + (k0 + (own ? tid : 0)) * ld + k0;
-  // a[p] = entries (2p, 2p+1) of this thread's row, for the packed FMA
-  uint64_t a[16];
-#pragma unroll
-  for (int p = 0; p < 16; ++p)
-    a[p] = pack2((own && 2 * p < w) ? rp[2 * p] : 0.f, (own && 2 * p + 1 < w) ? rp[2 * p + 1] : 0.f);
+// no warp waits for a single warp's factor. cb: 2 x 32 floats (ping-pong), db: 2 floats;
+// nthr: the panel's threads (a multiple of 32), all of which call this.
+__device__ __forceinline__ void panel_rows_factor(uint64_t (&a)[16], int w, int tid, int nthr,
+                                                  float* cb, float* db) {
   if (tid == 0) db[0] = lo_of(a[0]);
   asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
 #pragma unroll
@@ -106,6 +97,20 @@ __device__ __forceinline__ void mid_panel(float* As, int ld, int n, int k0, int 
       }
     }
   }
+}
+
+// The panel in shared memory: rows 0..rows-1 at P + t * ld (P = its element (k0, k0)).
+__device__ __forceinline__ void smem_panel(float* P, int ld, int rows, int w, int tid, float* cb,
+                                           float* db) {
+  const int nthr = (rows + 31) & ~31;
+  if (tid >= nthr) return;
+  const bool own = tid < rows;
+  float* rp = P + (own ? tid : 0) * ld;
+  uint64_t a[16];  // a[p] = entries (2p, 2p+1) of this thread's row, for the packed FMA
+#pragma unroll
+  for (int p = 0; p < 16; ++p)
+    a[p] = pack2((own && 2 * p < w) ? rp[2 * p] : 0.f, (own && 2 * p + 1 < w) ? rp[2 * p + 1] : 0.f);
+  panel_rows_factor(a, w, tid, nthr, cb, db);
   if (own) {
 #pragma unroll
     for (int p = 0; p < 16; ++p) {
@@ -200,7 +205,7 @@ __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
     __syncthreads();
     for (int k0 = 0; k0 < n; k0 += 32) {
       const int w = min(32, n - k0);
-      mid_panel(As, ld, n, k0, w, tid, cb, db);
+      smem_panel(As + k0 * ld + k0, ld, n - k0, w, tid, cb, db);
       __syncthreads();
       const int k1 = k0 + w;
       if (k1 < n) {
@@ -224,24 +229,177 @@ __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// 128 < n <= 256: one CTA of 512 threads per matrix. The matrix (256 KB) does not fit in
+// shared memory; it is worked on in place in L (a CTA's 256 KB stay in L2), and shared
+// memory holds the current panel's rows (stride 33). Per 32-wide panel: all threads stage
+// the panel's rows in shared memory (coalesced 128-byte row segments), the panel's warps
+// (up to 8) factor them with panel_rows_factor, all threads write the panel back to L, and
+// all 16 warps update the trailing lower triangle, C -= X X^T with X = the panel's rows
+// below its diagonal block, in column chunks of 64 (thread (tx, ty) of a 16 x 32
+// grid: columns tx + 16 c, c < 4, rows ty + 32 i, i < RI), reading C from the source (A for
+// the first panel, L after it) and writing L. Every lower entry of L is written by the first
+// panel and its update, so later panels read L only; A == L is allowed.
+constexpr int kWideMax = 256;
+constexpr int kWideThreads = 512;
+constexpr int kXld = 33;
+constexpr int kProws = kWideMax;
+
+// Columns [k1 + c0, k1 + c0 + 64) of the trailing matrix, rows from k1 + c0 down: RI row
+// groups of 32 (compile-time, so absent groups cost nothing).
+template <int RI>
+__device__ __forceinline__ void wide_update_t(const float* src, float* dst, int n, int k1,
+                                              int c0, int w, int tid, const float* X) {
+  const int tx = tid & 15, ty = tid >> 4;
+  const int m = n - k1;
+  int xr[RI], xc[4];
+#pragma unroll
+  for (int i = 0; i < RI; ++i) xr[i] = min(c0 + ty + 32 * i, m - 1) * kXld;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) xc[c] = min(c0 + tx + 16 * c, m - 1) * kXld;
+  // acc[i][q] = row group i x columns (2q, 2q + 1), packed; (i = 0, q = 1) lies above the
+  // diagonal for every thread and is skipped
+  uint64_t acc[RI][2];
+#pragma unroll
+  for (int i = 0; i < RI; ++i) acc[i][0] = acc[i][1] = 0ull;
+#pragma unroll 4
+  for (int k = 0; k < w; ++k) {
+    const uint64_t q0 = pack2(X[xc[0] + k], X[xc[1] + k]);
+    const uint64_t q1 = pack2(X[xc[2] + k], X[xc[3] + k]);
+#pragma unroll
+    for (int i = 0; i < RI; ++i) {
+      const float v = X[xr[i] + k];
+      const uint64_t vv = pack2(v, v);
+      acc[i][0] = ffma2_u64(vv, q0, acc[i][0]);
+      if (i > 0) acc[i][1] = ffma2_u64(vv, q1, acc[i][1]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RI; ++i)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (i == 0 && c >= 2) continue;
+      const int r = k1 + c0 + ty + 32 * i, col = k1 + c0 + tx + 16 * c;
+      if (r < n && col <= r) {
+        const int64_t o = int64_t(r) * n + col;
+        const uint64_t v = acc[i][c >> 1];
+        dst[o] = src[o] - ((c & 1) ? hi_of(v) : lo_of(v));
+      }
+    }
+}
+
+__device__ __forceinline__ void wide_update(const float* src, float* dst, int n, int k1, int c0,
+                                            int w, int tid, const float* X) {
+  switch ((n - k1 - c0 + 31) >> 5) {
+    case 1: wide_update_t<1>(src, dst, n, k1, c0, w, tid, X); break;
+    case 2: wide_update_t<2>(src, dst, n, k1, c0, w, tid, X); break;
+    case 3: wide_update_t<3>(src, dst, n, k1, c0, w, tid, X); break;
+    case 4: wide_update_t<4>(src, dst, n, k1, c0, w, tid, X); break;
+    case 5: wide_update_t<5>(src, dst, n, k1, c0, w, tid, X); break;
+    case 6: wide_update_t<6>(src, dst, n, k1, c0, w, tid, X); break;
+    default: wide_update_t<7>(src, dst, n, k1, c0, w, tid, X); break;
+  }
+}
+
+__global__ void __launch_bounds__(kWideThreads, 1)
+    wide_potrf_kernel(const float* A, float* L, int64_t batch, int n, int* info) {
+  griddep_wait();
+  griddep_launch();
+  extern __shared__ float sm[];
+  float* P = sm;  // the current panel's rows, stride kXld
+  float* cb = sm + kProws * kXld + 4 - (kProws * kXld) % 4;  // 16-byte aligned
+  float* db = cb + 64;
+  int* first = reinterpret_cast<int*>(db + 8);  // one per warp of the diagonal scan
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int64_t m = blockIdx.x; m < batch; m += gridDim.x) {
+    const float* Am = A + m * int64_t(n) * n;
+    float* Lm = L + m * int64_t(n) * n;
+    for (int r = warp; r < n; r += kWideThreads / 32)  // exact zeros above the diagonal
+      for (int c = r + 1 + lane; c < n; c += 32) Lm[int64_t(r) * n + c] = 0.f;
+    for (int k0 = 0; k0 < n; k0 += 32) {
+      const int w = min(32, n - k0);
+      const float* src = k0 == 0 ? Am : Lm;
+      const int rows = n - k0;
+      // the panel's rows into shared memory, one warp per 128-byte row segment (coalesced)
+      for (int e = tid; e < rows * 32; e += kWideThreads) {
+        const int r = e >> 5, c = e & 31;
+        if (c < w) P[r * kXld + c] = src[int64_t(k0 + r) * n + k0 + c];
+      }
+      __syncthreads();
+      smem_panel(P, kXld, rows, w, tid, cb, db);
+      __syncthreads();
+      for (int e = tid; e < rows * 32; e += kWideThreads) {  // the factored panel to L
+        const int r = e >> 5, c = e & 31;
+        if (c < w && c <= r) Lm[int64_t(k0 + r) * n + k0 + c] = P[r * kXld + c];
+      }
+      const int k1 = k0 + w;
+      if (k1 < n)  // X = the panel's rows below its diagonal block
+        for (int c0 = 0; c0 < n - k1; c0 += 64)
+          wide_update(src, Lm, n, k1, c0, w, tid, P + w * kXld);
+      __syncthreads();
+    }
+    if (info != nullptr) {
+      // the first diagonal entry that is not > 0 (warps 0..7 scan 32 rows each)
+      if (warp < 8) {
+        const int c = warp * 32 + lane;
+        const bool bad = c < n && !(Lm[int64_t(c) * n + c] > 0.f);
+        const unsigned mask = __ballot_sync(0xffffffffu, bad);
+        if (lane == 0) first[warp] = mask ? warp * 32 + __ffs(int(mask)) : 0;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int f = 0;
+        for (int q = 0; q < 8 && f == 0; ++q) f = first[q];
+        info[m] = f;
+      }
+    }
+    __syncthreads();  // the next matrix's panel overwrites X
+  }
+}
+
+size_t wide_smem_bytes() {
+  return (size_t(kProws * kXld + 4 - (kProws * kXld) % 4) + 64 + 8 + 8) * sizeof(float);
+}
+
 size_t mid_smem_bytes(int n) { return (size_t(mid_aux_offset(n)) + 72) * sizeof(float); }
 
 }  // namespace
 
 int g_mid_kernel = 1;
 
-bool use_mid(int64_t n) { return g_mid_kernel != 0 && n > 64 && n <= kMidMax; }
+// 64 < n <= 128: always. 128 < n <= 256: the wide kernel where the blocked schedule's
+// one-launch path is weak, i.e. a ragged last 64-wide tile (n % 64 != 0), for batches of at
+// most two CTAs per SM of a B200, or for n < 144 at any batch (A/B of library builds, us per
+// call, wide against blocked: b64n129 41 / 79, b64n200 77 / 116, b16n255 110 / 139,
+// b256n200 157 / 179, b148n160 48 / 88, b1024n129 304 / 346; but b1024n200 617 / 564,
+// b600n160 249 / 206, b300n255 359 / 346, and for n % 64 == 0 the blocked path wins:
+// b64n256 106 / 75, b64n192 63 / 51).
+constexpr int64_t kWideBatchMax = 2 * 148;
+bool use_mid(int64_t batch, int64_t n) {
+  if (g_mid_kernel == 0 || n <= 64 || n > kWideMax) return false;
+  if (n <= kMidMax) return true;
+  return n % 64 != 0 && (batch <= kWideBatchMax || n < 144);
+}
 
 cudaError_t prepare_mid() {
-  return cudaFuncSetAttribute(mid_potrf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(mid_smem_bytes(kMidMax)));
+  cudaError_t e = cudaFuncSetAttribute(mid_potrf_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(mid_smem_bytes(kMidMax)));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(wide_potrf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(wide_smem_bytes()));
 }
 
 int launch_mid(const float* A, float* L, int64_t batch, int n, int* info, cudaStream_t q) {
-  if (n <= 64 || n > kMidMax) return CHOL_ERR_UNSUPPORTED;
+  if (n <= 64 || n > kWideMax) return CHOL_ERR_UNSUPPORTED;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (n > kMidMax) {
+    const int64_t grid = std::min<int64_t>(batch, int64_t(sms) * 16);
+    return status_from(launch_pdl(wide_potrf_kernel, dim3(unsigned(grid)), dim3(kWideThreads),
+                                  wide_smem_bytes(), q, true, A, L, batch, n, info));
+  }
   const int64_t grid = std::min<int64_t>(batch, int64_t(sms) * kMidCtasPerSm * 16);
   return status_from(launch_pdl(mid_potrf_kernel, dim3(unsigned(grid)), dim3(kMidThreads),
                                 mid_smem_bytes(n), q, true, A, L, batch, n, info));

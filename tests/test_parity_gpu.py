@@ -286,10 +286,13 @@ def test_single_panel_sizes(batch, n, lam, panel_inverse):
         lib.chol_set_option(_lib.CHOL_OPT_PANEL_INVERSE, 1)
 
 
-# 64 < n <= 128: the shared-memory kernel (one CTA per matrix) against the oracle, and the
-# blocked schedule (CHOL_OPT_MID_KERNEL = 0, through the library-workspace C entry) for the
-# same inputs within the same bounds
-@pytest.mark.parametrize("batch,n", [(256, 128), (7, 65), (33, 100), (5, 127), (600, 96)])
+# 64 < n <= 128: the shared-memory kernel (one CTA per matrix), and ragged 128 < n <= 256:
+# the wide kernel (one 512-thread CTA per matrix, the matrix in L), against the oracle, and
+# the blocked schedule (CHOL_OPT_MID_KERNEL = 0, through the library-workspace C entry) for
+# the same inputs within the same bounds
+@pytest.mark.parametrize("batch,n", [(256, 128), (7, 65), (33, 100), (5, 127), (600, 96),
+                                     (64, 129), (16, 255), (296, 200), (1024, 130), (3, 161),
+                                     (9, 250)])
 def test_mid_kernel_sizes(batch, n):
     lib = _lib.load()
     a, cond = inputs.spectral(batch, n, 1e3, 8500 + n)
@@ -308,14 +311,16 @@ def test_mid_kernel_sizes(batch, n):
         assert res["ok"], (name, batch, n, res)
 
 
-def test_mid_kernel_not_spd_info():
-    """info from the shared-memory kernel: the first failing column, as LAPACK reports it
-    (in the first panel, a later panel and the last column)."""
-    a, _ = inputs.spectral(5, 100, 10.0, 98, device=DEV)
+@pytest.mark.parametrize("n", [100, 200])
+def test_mid_kernel_not_spd_info(n):
+    """info from the shared-memory kernel (n = 100) and the wide kernel (n = 200): the first
+    failing column, as LAPACK reports it (in the first panel, a later panel and the last
+    column)."""
+    a, _ = inputs.spectral(5, n, 10.0, 98, device=DEV)
     a = a.clone()
     a[1, 10, 10] = -1.0
-    a[2, 70, 70] = -5.0
-    a[4, 99, 99] = -3.0
+    a[2, n - 30, n - 30] = -5.0
+    a[4, n - 1, n - 1] = -3.0
     l, info = cholesky_ex(a)
     want = torch.linalg.cholesky_ex(a.cpu()).info
     assert torch.equal(info.cpu(), want), (info.cpu(), want)

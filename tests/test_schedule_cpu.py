@@ -2,7 +2,7 @@
 
 chol_launch_count and chol_workspace_bytes are pure host logic; they follow the schedules
 the blocked path picks: one small-kernel launch for n <= 64, one shared-memory-kernel launch
-for n <= 128; for one panel, the whole matrix
+for n <= 128, one wide-kernel launch for a ragged 128 < n <= 256 (small batches); for one panel, the whole matrix
 in one diagonal-block launch while batch * n^3 is small, else the left-looking chain (a zero
 fill, then per block column a factor, a left-looking update and a solve; 128-wide block
 columns when n % 128 == 0, 64-wide otherwise or with CHOL_OPT_CHAIN_WIDTH = 64); for several
@@ -29,7 +29,10 @@ ROOT = Path(__file__).resolve().parents[1]
     (60, 1024, 47),         # batch < 256: 64-wide chain: 1 + 16 + 15 + 15
     (256, 1024, 22),        # 128-wide chain: 8 + 7 + 7
     (400, 320, 14),         # n % 128 != 0: 64-wide chain: 1 + 5 + 4 + 4
-    (3, 200, 11),           # chain with a ragged last block: 1 + 4 + 3 + 3
+    (3, 200, 1),            # ragged 128 < n <= 256, small batch: one wide-kernel launch
+    (600, 200, 11),         # the same n at a large batch: the 64-wide chain, 1 + 4 + 3 + 3
+    (1024, 130, 1),         # n < 144: the wide kernel at any batch
+    (64, 192, 2),           # n % 64 == 0: the one-launch diagonal-block path (+ copy)
     (1, 2048, 16),          # 3 x (block, solve, split, trailing) + last block + copy,
                             # + 2 look-ahead splits (automatic for n <= 8192)
     (1, 2100, 35),          # 768-wide panels: 2 full ones (block, solve, split, trailing; one
@@ -68,10 +71,11 @@ def test_chain_width_option():
 
 
 def test_mid_sizes_take_one_launch_and_no_workspace():
-    """64 < n <= 128: one launch of the shared-memory kernel, no workspace; with
-    CHOL_OPT_MID_KERNEL = 0 the blocked schedule (and its workspace) comes back."""
+    """64 < n <= 128: one launch of the shared-memory kernel, no workspace; the same for the
+    wide kernel's ragged 128 < n <= 256; with CHOL_OPT_MID_KERNEL = 0 the blocked schedule
+    (and its workspace) comes back."""
     lib = _lib.load()
-    for b, n in ((256, 128), (7, 65), (33, 100)):
+    for b, n in ((256, 128), (7, 65), (33, 100), (256, 130), (296, 255), (2048, 143)):
         assert int(lib.chol_launch_count(b, n)) == 1
         assert int(lib.chol_workspace_bytes(b, n)) == 0
     assert lib.chol_set_option(_lib.CHOL_OPT_MID_KERNEL, 2) == _lib.CHOL_ERR_INVALID_ARG
@@ -80,9 +84,12 @@ def test_mid_sizes_take_one_launch_and_no_workspace():
         assert int(lib.chol_launch_count(256, 128)) == 2    # diagonal-block launch + copy
         assert int(lib.chol_workspace_bytes(256, 128)) > 0
         assert int(lib.chol_launch_count(7, 100)) > 1
+        assert int(lib.chol_launch_count(7, 200)) > 1
     finally:
         lib.chol_set_option(_lib.CHOL_OPT_MID_KERNEL, 1)
-    assert int(lib.chol_launch_count(256, 130)) > 1           # past the mid range
+    assert int(lib.chol_launch_count(297, 255)) > 1           # past the wide kernel's batches
+    assert int(lib.chol_launch_count(8, 256)) > 1             # n % 64 == 0: blocked
+    assert int(lib.chol_launch_count(8, 257)) > 1             # past n = 256
 
 
 def test_workspace_regions():

@@ -53,7 +53,7 @@ def test_no_alloc_matches_allocating_entry_point(batch, n):
 
 def test_no_alloc_rejects_sizes_beyond_its_scratch():
     lib = _lib.load()
-    batch, n = 257, 130  # 257 inverse blocks of 16 KiB > the fixed 4 MiB scratch
+    batch, n = 257, 192  # blocked path: 257 inverse blocks of 16 KiB > the fixed 4 MiB scratch
     a = torch.eye(n, device=DEV).expand(batch, n, n).contiguous()
     out = torch.empty_like(a)
     st = lib.chol_potrf_batched_noalloc_f32(ctypes.c_void_p(a.data_ptr()),

@@ -281,10 +281,20 @@ class QueuePair:
             self.caller.wait_stream(q)
 
 
-# (chain, bulk) GEMM CTA caps of the two queues over several ranks; 148 - 132 = 16 SMs stay
-# free for NCCL's kernels. At 2 GPUs, n = 32768: 54.7 ms in order, 51.3 ms at (40, 92),
-# 51.9 at (32, 100), 52.1 at (48, 84), 56.2 at (24, 108), 60.4 at (64, 64), 54.0 uncapped.
-AUTO_QUEUES = (40, 92)
+# (chain, bulk) GEMM CTA caps of the two queues by rank count; 148 - 132 = 16 SMs stay free
+# for NCCL's kernels. Each rank's bulk work shrinks as 1/ranks while the chain's does not,
+# so the chain's share grows with the rank count. n = 32768: at 2 GPUs 54.7 ms in order,
+# 51.3 at (40, 92), 51.9 at (32, 100), 52.1 at (48, 84), 56.2 at (24, 108), 60.4 at
+# (64, 64), 54.0 uncapped; at 4 GPUs 43.0 in order, 40.9 at (40, 92), 38.1 at (56, 76),
+# 39.8 at (72, 60). Above 4 ranks the next step of the same trend.
+def auto_queues(world: int) -> tuple[int, int] | None:
+    if world <= 1:
+        return None
+    if world == 2:
+        return (40, 92)
+    if world <= 4:
+        return (56, 76)
+    return (72, 60)
 
 
 def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=None, ops=None,
@@ -300,15 +310,14 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
     steps of the chain to finish in. ``paired`` defers every other bulk update and applies
     two panels at once (K = 2 bs). ``queues`` = (chain, bulk) GEMM CTA caps of the two
     queues (``QueuePair``); None runs everything in order on the caller's queue; "auto" =
-    ``AUTO_QUEUES`` over several ranks and None on one (there the bulk is the whole
-    trailing update and every SM it gives up costs more than the overlap wins: n = 32768
-    on one GPU 86.1 ms in order, 90.0 ms at (32, 100)). Returns ``local`` (now this rank's
-    columns of L).
+    ``auto_queues(world)``: None on one rank (there the bulk is the whole trailing update
+    and every SM it gives up costs more than the overlap wins: n = 32768 on one GPU 86.1 ms
+    in order, 90.0 ms at (32, 100)). Returns ``local`` (now this rank's columns of L).
     """
     if isinstance(queues, str):
         if queues != "auto":
             raise ValueError(f"queues: {queues!r}")
-        queues = AUTO_QUEUES if lay.world > 1 else None
+        queues = auto_queues(lay.world)
     if ops is None:
         ops = CudaOps(local.device)
     n, bs = lay.n, lay.bs

@@ -209,3 +209,14 @@ def test_batch_sharded_single_rank_and_argument_checks():
 
     with pytest.raises(ValueError, match="every rank"):
         factor_batch_sharded(a[:1], 1, 16, TwoRanks(), factor=_cpu_factor)
+
+
+def test_auto_queue_caps_follow_the_rank_count():
+    """One rank runs in order; over several ranks the chain's share of the SMs grows with the
+    rank count (each rank's bulk work shrinks as 1/ranks), and 16 SMs stay free for NCCL."""
+    from linalg_kernels_b200.distributed import auto_queues
+
+    assert auto_queues(1) is None
+    caps = [auto_queues(w) for w in (2, 4, 8)]
+    assert [c[0] for c in caps] == sorted(c[0] for c in caps)
+    assert all(c[0] + c[1] == 132 for c in caps)

@@ -279,6 +279,17 @@ CHOL_API int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, fl
 CHOL_API int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w, float* out,
                                       int flags, int* info, void* queue);
 
+/* The diagonal-block step of chol_panel_potrf_out_f32 alone: factors the w x w block at L
+   (row stride ld) in place with one launch and writes V = inv(L11) to V (w x w floats,
+   row-major, contiguous, disjoint from L; the entries above its diagonal are zero), so
+   that a caller can solve the rows below as X = A21 V^T (chol_gemm_nt_f32) wherever they
+   are: the multi-GPU driver sends the unfactored panel while its owner factors the block,
+   then sends L11 and V, and every rank solves its copy. w: a multiple of 64, <= 1024;
+   16-byte aligned rows. info (nullable, one int): first failing column (1-based) or 0.
+   Uses the same cached scratch as chol_panel_potrf_f32 (calls on different queues race). */
+CHOL_API int chol_diag_potrf_inv_f32(float* L, int64_t ld, int64_t w, float* V, int* info,
+                                     void* queue);
+
 /* chol_gemm_nt_f32 for one matrix whose columns are stored block-cyclically: local column c
    of C (and row c of Q) stands for global column c + (c / col_block) * (col_stride -
    col_block), and lower_only compares that global column with the row. One launch updates

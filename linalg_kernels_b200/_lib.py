@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple] = {
                                 _vp, _i64, _i64, _f32, _f32, _i64, _int, _vp]),
     "chol_panel_potrf_f32": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "chol_panel_potrf_out_f32": (_int, [_vp, _i64, _i64, _i64, _vp, _int, _vp, _vp]),
+    "chol_diag_potrf_inv_f32": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "chol_gemm_nt_cyclic_f32": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _f32,
                                        _f32, _i64, _int, _i64, _i64, _vp]),
     "chol_validate_work_bytes": (_sz, [_i64, _i64]),

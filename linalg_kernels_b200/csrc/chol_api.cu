@@ -963,6 +963,31 @@ int chol_panel_potrf_f32(float* L, int64_t ld, int64_t m, int64_t w, float* Tinv
   return CHOL_OK;
 }
 
+int chol_diag_potrf_inv_f32(float* L, int64_t ld, int64_t w, float* V, int* info, void* queue) {
+  if (L == nullptr || V == nullptr || w < 0 || ld < w) return CHOL_ERR_INVALID_ARG;
+  if (w == 0) return CHOL_OK;
+  if (w % kBlock || w > 16 * kBlock || ld % 4 || (reinterpret_cast<uintptr_t>(L) & 15) ||
+      (reinterpret_cast<uintptr_t>(V) & 15))
+    return CHOL_ERR_UNSUPPORTED;
+  const uintptr_t v0 = reinterpret_cast<uintptr_t>(V), v1 = v0 + uintptr_t(w * w) * 4;
+  const uintptr_t l0 = reinterpret_cast<uintptr_t>(L);
+  if (v0 < l0 + uintptr_t((w - 1) * ld + w) * 4 && l0 < v1) return CHOL_ERR_INVALID_ARG;
+  int dev = 0, st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHOL_ERR_DEVICE;
+  if ((st = prepare_device(dev))) return st;
+  cudaStream_t q = static_cast<cudaStream_t>(queue);
+  const size_t fbytes = kDiagFlags * sizeof(int) + 256;
+  char* base = static_cast<char*>(panel_scratch(dev, fbytes));
+  if (base == nullptr) return CHOL_ERR_WORKSPACE;
+  int* flags = reinterpret_cast<int*>(base);
+  unsigned* ticket = reinterpret_cast<unsigned*>(flags + kDiagFlags);
+  if (cudaMemsetAsync(base, 0, fbytes, q) != cudaSuccess ||
+      cudaMemsetAsync(V, 0, size_t(w) * size_t(w) * sizeof(float), q) != cudaSuccess)
+    return CHOL_ERR_LAUNCH;
+  return launch_diag_block(L, 0, ld, V, 0, w, int(w / kBlock), true, flags, ticket, 1, info, 0,
+                           1, q);
+}
+
 int chol_panel_potrf_out_f32(float* L, int64_t ld, int64_t m, int64_t w, float* out, int flags,
                              int* info, void* queue) {
   if (flags & ~CHOL_PANEL_OUT_ONLY) return CHOL_ERR_INVALID_ARG;

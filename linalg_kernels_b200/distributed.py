@@ -124,6 +124,19 @@ class CudaOps:
     def queues(self, chain_ctas: int, bulk_ctas: int) -> "QueuePair":
         return QueuePair(self, chain_ctas, bulk_ctas)
 
+    def diag_potrf_inv(self, block: torch.Tensor, v: torch.Tensor,
+                       info: torch.Tensor | None) -> bool:
+        """Factor the w x w block view in place and write v = inv(L11) (w x w, contiguous).
+        False when the one-launch form does not take the shape (nothing done)."""
+        w = block.shape[0]
+        st = self.lib.chol_diag_potrf_inv_f32(
+            ctypes.c_void_p(block.data_ptr()), _rowmajor(block), w, ctypes.c_void_p(v.data_ptr()),
+            ctypes.c_void_p(info.data_ptr()) if info is not None else None, self._q())
+        if st == _lib.CHOL_ERR_UNSUPPORTED:
+            return False
+        _lib.check(st, "chol_diag_potrf_inv_f32")
+        return True
+
     def potrf_block(self, diag: torch.Tensor, tinv: torch.Tensor, info: torch.Tensor | None):
         """Factor diag (kb x kb view, kb <= 64) in place; tinv (64 x 64) <- inv(L)."""
         ld = _rowmajor(diag)
@@ -286,7 +299,8 @@ class QueuePair:
 # so the chain's share grows with the rank count. n = 32768: at 2 GPUs 54.7 ms in order,
 # 51.3 at (40, 92), 51.9 at (32, 100), 52.1 at (48, 84), 56.2 at (24, 108), 60.4 at
 # (64, 64), 54.0 uncapped; at 4 GPUs 43.0 in order, 40.9 at (40, 92), 38.1 at (56, 76),
-# 39.8 at (72, 60). Above 4 ranks the next step of the same trend.
+# 39.8 at (72, 60); at 8 GPUs 34.3 at (88, 44) and 35.9 at (56, 76), steady over repeats,
+# while (72, 60) varied from 34 to 42 ms between repeats.
 def auto_queues(world: int) -> tuple[int, int] | None:
     if world <= 1:
         return None
@@ -294,12 +308,13 @@ def auto_queues(world: int) -> tuple[int, int] | None:
         return (40, 92)
     if world <= 4:
         return (56, 76)
-    return (72, 60)
+    return (88, 44)
 
 
 def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=None, ops=None,
                         info: torch.Tensor | None = None, paired: bool = True,
-                        queues: tuple[int, int] | None | str = "auto") -> torch.Tensor:
+                        queues: tuple[int, int] | None | str = "auto",
+                        split_send: bool | None = None) -> torch.Tensor:
     """Factor in place the block-column-cyclic matrix whose local columns are ``local``.
 
     ``pg`` is ``torch.distributed`` (or None for a single rank); ``ops`` defaults to
@@ -312,7 +327,20 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
     queues (``QueuePair``); None runs everything in order on the caller's queue; "auto" =
     ``auto_queues(world)``: None on one rank (there the bulk is the whole trailing update
     and every SM it gives up costs more than the overlap wins: n = 32768 on one GPU 86.1 ms
-    in order, 90.0 ms at (32, 100)). Returns ``local`` (now this rank's columns of L).
+    in order, 90.0 ms at (32, 100)).
+
+    ``split_send`` (off by default): the
+    owner broadcasts block ``j+1`` as soon as its look-ahead update is done, unfactored, and
+    factors only its diagonal block meanwhile (``chol_diag_potrf_inv_f32``: L11 and
+    V = inv(L11)); a second, small broadcast sends L11 and V, and every rank solves the rows
+    below itself (X = A21 V^T). The large send then overlaps the diagonal factor instead of
+    following the whole panel factor. The owner keeps the block it sends in a contiguous
+    buffer (copied out of its columns after the block's last update before the look-ahead),
+    so the send needs no packing. Every rank computes the same products as the owner would,
+    so the factor is bitwise that of the unsplit schedule. It measured no faster (n = 32768:
+    2 GPUs 52.6 against 50.8 ms, 4 GPUs 38.0-41.2 against 38.5-40.1, 8 GPUs 33.3-37.0
+    against 34.3-36.1): the solve moves onto every rank's chain, and at 2-4 GPUs the bulk,
+    not the chain, sets the time. Returns ``local`` (now this rank's columns of L).
     """
     if isinstance(queues, str):
         if queues != "auto":
@@ -320,6 +348,8 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
         queues = auto_queues(lay.world)
     if ops is None:
         ops = CudaOps(local.device)
+    if split_send is None:
+        split_send = False
     n, bs = lay.n, lay.bs
     nb = lay.nblocks
     dev = local.device
@@ -328,9 +358,13 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
     nbuf = 4  # panel j's buffer is rewritten by panel j + 4 (its readers end at step j + 1)
     bufs = [torch.empty(n * bs, dtype=local.dtype, device=dev) for _ in range(nbuf)]
     combs = [torch.empty(n * 2 * bs, dtype=local.dtype, device=dev) for _ in range(2 if paired else 0)]
+    # split_send: the sent (unfactored) block columns and [L11 | V] of the last two blocks
+    raws = [torch.empty(n * bs, dtype=local.dtype, device=dev) for _ in range(2 if split_send else 0)]
+    svs = [torch.empty(2 * bs * bs, dtype=local.dtype, device=dev) for _ in range(2 if split_send else 0)]
     make = getattr(ops, "queues", None)
     qs = make(*queues) if (queues is not None and make is not None) else _OneQueue()
     owned = lay.owned()
+    multi = pg is not None and lay.world > 1
 
     def mine(t):
         return t < nb and lay.owner(t) == lay.rank
@@ -339,35 +373,95 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
         rows = n - j * bs
         return bufs[j % nbuf][: rows * lay.width(j)].view(rows, lay.width(j))
 
+    def raw_view(t):
+        rows = n - t * bs
+        return raws[t % 2][: rows * lay.width(t)].view(rows, lay.width(t))
+
+    def sv_view(t):
+        w = lay.width(t)
+        return svs[t % 2][: 2 * w * w].view(2, w, w)
+
+    def local_block(t):
+        lc = lay.local_col(t)
+        return local[t * bs:, lc:lc + lay.width(t)]
+
+    def bcast(x, t):
+        return pg.broadcast(x, src=_global_rank(pg, group, lay.owner(t)), group=group,
+                            async_op=True)
+
     bulk_done = {}  # step -> event after the bulk queue's work of that step
 
     def publish(j):
         """Chain queue: the owner factors block j (fully updated) into its send buffer; every
         rank joins the broadcast. The owner copies the solved rows back into its own columns
         after the broadcast is issued, so that copy runs beside the send. Returns the work
-        handle."""
+        handles."""
         qs.wait(bulk_done.get(j - nbuf + 1))  # the buffer's previous panel is read out
         pv = panel_view(j)
         back = None
         if mine(j):
             back = _factor_panel(local, lay, j, ops, tinv, info, out=pv, defer_copy=True)
-        handle = None
-        if pg is not None and lay.world > 1:
-            handle = pg.broadcast(pv, src=_global_rank(pg, group, lay.owner(j)), group=group,
-                                  async_op=True)
+        handles = [bcast(pv, j)] if multi else []
         if back is not None:
             back[0].copy_(back[1])
-        return handle
+        return handles
+
+    def publish_split(t):
+        """Chain queue, split_send: send block t unfactored, factor its diagonal block beside
+        the send, then send [L11 | V]. The last block (no rows below) is factored whole by
+        its owner and sent once."""
+        r = raw_view(t)
+        handles = []
+        if t == nb - 1:
+            if mine(t):
+                ops.panel_potrf(r, tinv, info)
+            return [bcast(r, t)] if multi else []
+        if multi:
+            handles.append(bcast(r, t))
+        sv = sv_view(t)
+        if mine(t):
+            sv[0].copy_(r[: lay.width(t)])
+            if not ops.diag_potrf_inv(sv[0], sv[1], info):
+                raise RuntimeError("chol_diag_potrf_inv_f32 does not take this block")
+        if multi:
+            handles.append(bcast(sv, t))
+        return handles
+
+    def finish_split(t):
+        """Chain queue, split_send, once block t's sends have arrived: panel t = [L11; A21 V^T]
+        into its buffer (the owner copies it into its own columns later in the step, after
+        the next block's sends are issued)."""
+        qs.wait(bulk_done.get(t - nbuf + 1))  # the buffer's previous panel is read out
+        pv, r, w = panel_view(t), raw_view(t), lay.width(t)
+        if t == nb - 1:
+            pv.copy_(r)
+        else:
+            sv = sv_view(t)
+            pv[:w].copy_(sv[0])
+            ops.gemm_nt(pv[w:], r[w:], sv[1], 1.0, 0.0, False)
+
+    def stage(t):
+        """Owner, split_send: block t (all updates before the look-ahead applied) into its
+        contiguous send buffer, where the look-ahead update then applies."""
+        if mine(t):
+            raw_view(t).copy_(local_block(t))
 
     with qs.on("chain"):
-        work = publish(0)
+        if split_send:
+            stage(0)
+            stage(1)
+            work = publish_split(0)
+        else:
+            work = publish(0)
     pending = None  # step whose bulk update is deferred to the next step (paired)
     ncomb = 0  # combined buffers alternate: one is read while the next is written
     for j in range(nb):
         l1, l2 = j + 1, j + 2
         with qs.on("chain"):
-            if work is not None:
-                work.wait()
+            for h in work:
+                h.wait()
+            if split_send:
+                finish_split(j)
             ready = qs.record()
         rest = [t for t in owned if t > l2]
         defer = paired and pending is None and l2 + 1 < nb
@@ -390,14 +484,25 @@ def factor_block_cyclic(local: torch.Tensor, lay: CyclicLayout, pg=None, group=N
             bulk_done[j] = qs.record()
         with qs.on("chain"):
             if mine(l1):
-                _update_blocks(local, lay, [l1], j * bs, panel_view(j), ops)
-            work = publish(l1) if l1 < nb else None
+                if split_send:
+                    p = panel_view(j)[bs:]  # rows from block l1's first row
+                    ops.gemm_nt(raw_view(l1), p, p[: lay.width(l1)], -1.0, 1.0, True)
+                else:
+                    _update_blocks(local, lay, [l1], j * bs, panel_view(j), ops)
+            if l1 < nb:
+                work = publish_split(l1) if split_send else publish(l1)
+            else:
+                work = []
+            if split_send and mine(j):
+                local_block(j).copy_(panel_view(j))  # panel j into the owner's columns
             if mine(l2):
                 qs.wait(pre)  # block l2 left the bulk set at this step
                 if comb is not None:
                     _update_blocks(local, lay, [l2], l2 * bs, comb, ops)
                 else:
                     _update_blocks(local, lay, [l2], j * bs, panel_view(j), ops)
+                if split_send:
+                    stage(l2)
         bulk_done.pop(j - nbuf, None)
         pending = j if defer else None
     qs.join()

@@ -31,6 +31,12 @@ class CpuOps:
         if panel.shape[0] > w:
             panel[w:] = torch.linalg.solve_triangular(l, panel[w:].T, upper=False).T
 
+    def diag_potrf_inv(self, block, v, info):
+        l = torch.linalg.cholesky(torch.tril(block) + torch.tril(block, -1).T)
+        block.copy_(l)
+        v.copy_(torch.linalg.inv(l))
+        return True
+
     def cyclic_update(self, c, p, block, stride):
         nc = c.shape[1]
         for b in range(0, nc, block):
@@ -59,7 +65,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, n, bs, seed, out_dir, paired=True):
+def _worker(rank, world, port, n, bs, seed, out_dir, paired=True, split=None):
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -69,22 +75,28 @@ def _worker(rank, world, port, n, bs, seed, out_dir, paired=True):
         a = _matrix(n, seed)
         lay = CyclicLayout(n, world, rank, bs)
         local = scatter_block_cyclic(a, lay)
-        factor_block_cyclic(local, lay, pg=dist, ops=CpuOps(), paired=paired)
+        factor_block_cyclic(local, lay, pg=dist, ops=CpuOps(), paired=paired, split_send=split)
         torch.save(local, os.path.join(out_dir, f"part{rank}.pt"))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,n,bs,paired", [(2, 300, 64, True), (3, 260, 32, True),
-                                               (2, 128, 64, True), (3, 260, 32, False),
-                                               (4, 520, 32, True)])
-def test_block_cyclic_gloo_matches_cholesky(tmp_path, world, n, bs, paired):
+@pytest.mark.parametrize("world,n,bs,paired,split", [(2, 300, 64, True, None),
+                                                     (3, 260, 32, True, None),
+                                                     (2, 128, 64, True, None),
+                                                     (3, 260, 32, False, None),
+                                                     (4, 520, 32, True, None),
+                                                     (3, 260, 32, True, True),
+                                                     (2, 300, 64, False, True),
+                                                     (4, 520, 32, True, True)])
+def test_block_cyclic_gloo_matches_cholesky(tmp_path, world, n, bs, paired, split):
     # paired: every other update of the blocks right of the look-ahead block is deferred
-    # and applied for two panels at once
+    # and applied for two panels at once; split (split_send, off by default): each block is
+    # sent unfactored, then [L11 | inv(L11)], and every rank solves the rows below itself
     port = _free_port()
-    mp.spawn(_worker, args=(world, port, n, bs, 11 + n, str(tmp_path), paired), nprocs=world,
-             join=True)
+    mp.spawn(_worker, args=(world, port, n, bs, 11 + n, str(tmp_path), paired, split),
+             nprocs=world, join=True)
     parts = [torch.load(tmp_path / f"part{r}.pt") for r in range(world)]
     l = gather_block_cyclic(parts, n, world, bs).double()
     a = _matrix(n, 11 + n).double()
@@ -95,12 +107,13 @@ def test_block_cyclic_gloo_matches_cholesky(tmp_path, world, n, bs, paired):
     assert rel < 1e-5, rel
 
 
-def test_single_rank_without_process_group():
+@pytest.mark.parametrize("split", [False, True])
+def test_single_rank_without_process_group(split):
     n, bs = 200, 64
     a = _matrix(n, 5)
     lay = CyclicLayout(n, 1, 0, bs)
     local = scatter_block_cyclic(a, lay)
-    factor_block_cyclic(local, lay, pg=None, ops=CpuOps())
+    factor_block_cyclic(local, lay, pg=None, ops=CpuOps(), split_send=split)
     ref = torch.linalg.cholesky(a.double())
     assert (local.double() - ref).abs().max().item() < 1e-4
 

@@ -52,6 +52,60 @@ def test_cyclic_queue_pair_matches_one_queue(queues, paired):
     assert oracle.check_factor(a.numpy(), l, l_ref=l_or, cond=cond.numpy())["ok"]
 
 
+@pytest.mark.parametrize("n", [2560, 700])
+def test_cyclic_split_send_matches_unsplit(n):
+    """split_send (each block sent unfactored, then [L11 | inv(L11)], every rank solving the
+    rows below itself) computes bitwise what the owner-factors-the-panel schedule computes:
+    the same diagonal-block kernel and the same solve GEMM, on contiguous copies. n = 700
+    ends with a 188-wide block (factored whole by its owner)."""
+    bs = 256
+    a, cond = inputs.covariance(1, n, 0.5, 4300 + n)
+    lay = CyclicLayout(n, 1, 0, bs)
+    base = scatter_block_cyclic(a[0].to(DEV), lay)
+    one = factor_block_cyclic(base.clone(), lay, pg=None, split_send=False)
+    two = factor_block_cyclic(base.clone(), lay, pg=None, split_send=True)
+    three = factor_block_cyclic(base.clone(), lay, pg=None, split_send=True, queues=(56, 76))
+    torch.cuda.synchronize()
+    assert torch.equal(one, two)
+    assert torch.equal(one, three)
+    l = gather_block_cyclic([two], n, 1, bs).cpu().numpy()[None]
+    l_or, _ = oracle.potrf(a.numpy())
+    assert oracle.check_factor(a.numpy(), l, l_ref=l_or, cond=cond.numpy())["ok"]
+
+
+@pytest.mark.parametrize("w", [256, 512, 64])
+def test_diag_potrf_inv(w):
+    """chol_diag_potrf_inv_f32: the block factored in place equals the top block of the
+    one-launch panel factor (bitwise), and V = inv(L11) to FP32 accuracy."""
+    from linalg_kernels_b200 import _lib
+    from linalg_kernels_b200.distributed import CudaOps
+
+    ops = CudaOps(torch.device(DEV))
+    m = w + 300
+    a, _ = inputs.covariance(1, m, 0.5, 900 + w)
+    base = torch.tril(a[0]).to(DEV).contiguous()
+    ref = base.clone()
+    out = torch.empty(m, w, device=DEV)
+    assert ops.panel_potrf_out(ref[:, :w], out, None)
+    blk = base[:w, :w].clone()
+    v = torch.full((w, w), float("nan"), device=DEV)
+    info = torch.full((1,), -1, dtype=torch.int32, device=DEV)
+    assert ops.diag_potrf_inv(blk, v, info)
+    torch.cuda.synchronize()
+    assert int(info.item()) == 0
+    assert torch.equal(torch.tril(blk), torch.tril(ref[:w, :w]))
+    assert torch.equal(torch.triu(v, 1), torch.zeros_like(v))
+    eye = torch.tril(blk).double() @ v.double()
+    assert (eye - torch.eye(w, device=DEV, dtype=torch.float64)).abs().max().item() < 1e-3
+    lib = _lib.load()
+    assert lib.chol_diag_potrf_inv_f32(ctypes.c_void_p(blk.data_ptr()), w, w - 32,
+                                       ctypes.c_void_p(v.data_ptr()), None, None) \
+        == _lib.CHOL_ERR_UNSUPPORTED  # w not a multiple of 64
+    assert lib.chol_diag_potrf_inv_f32(ctypes.c_void_p(blk.data_ptr()), w, w,
+                                       ctypes.c_void_p(blk.data_ptr()), None, None) \
+        == _lib.CHOL_ERR_INVALID_ARG  # V overlaps L
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_cyclic_emulated_ranks_on_one_gpu(world):
     """Each emulated rank's columns factored by the same schedule must equal the
@@ -72,7 +126,7 @@ def test_cyclic_emulated_ranks_on_one_gpu(world):
     assert torch.equal(gather_block_cyclic(parts, n, world, bs), want)
 
 
-def _nccl_worker(rank, world, port, n, bs, seed, out_dir):
+def _nccl_worker(rank, world, port, n, bs, seed, out_dir, split=False):
     import os
 
     import torch.distributed as dist
@@ -90,7 +144,7 @@ def _nccl_worker(rank, world, port, n, bs, seed, out_dir):
         a, _ = inputs.covariance(1, n, 0.5, seed)
         lay = CyclicLayout(n, world, rank, bs)
         local = scatter_block_cyclic(a[0].to(f"cuda:{rank}"), lay)
-        factor_block_cyclic(local, lay, pg=dist)
+        factor_block_cyclic(local, lay, pg=dist, split_send=split)
         torch.cuda.synchronize()
         torch.save(local.cpu(), os.path.join(out_dir, f"part{rank}.pt"))
         dist.barrier(device_ids=[rank])
@@ -99,7 +153,8 @@ def _nccl_worker(rank, world, port, n, bs, seed, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_cyclic_two_ranks_nccl(tmp_path):
+@pytest.mark.parametrize("split", [False, True])
+def test_cyclic_two_ranks_nccl(tmp_path, split):
     import socket
 
     import torch.multiprocessing as mp
@@ -108,7 +163,8 @@ def test_cyclic_two_ranks_nccl(tmp_path):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     n, bs = 1536, 256
-    mp.spawn(_nccl_worker, args=(2, port, n, bs, 4242, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_nccl_worker, args=(2, port, n, bs, 4242, str(tmp_path), split), nprocs=2,
+             join=True)
     parts = [torch.load(tmp_path / f"part{r}.pt") for r in range(2)]
     l = gather_block_cyclic(parts, n, 2, bs).numpy()[None]
     a, cond = inputs.covariance(1, n, 0.5, 4242)

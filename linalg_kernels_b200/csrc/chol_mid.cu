@@ -48,74 +48,112 @@ __device__ __forceinline__ float mid_rsqrt(float x) {
   return y;
 }
 
-// The panel's warps (rows k0..n-1, one row per thread: thread t holds row k0 + t, columns
-// k0..k0+w-1, in registers): the w columns of the panel, right-looking. Per column j: every
-// thread reads the pivot d from shared memory (the owner of row k0 + j prepared it in the
-// previous column from its own registers: look-ahead) and scales its entry by r = rsqrt(d)
-// (the diagonal row gets d r = sqrt(d)); the diagonal block's rows below j publish their
-// entry of column j; one barrier of the panel's warps; then every row below j takes the
-// rank-1 update of its remaining columns, reading the published column as shared-memory
-// broadcasts. This factors the diagonal block and solves the rows below it in one pass, so
-// no warp waits for a single warp's factor. cb: 2 x 32 floats (ping-pong), db: 2 floats;
-// nthr: the panel's threads (a multiple of 32), all of which call this.
-__device__ __forceinline__ void panel_rows_factor(uint64_t (&a)[16], int w, int tid, int nthr,
-                                                  float* cb, float* db) {
-  if (tid == 0) db[0] = lo_of(a[0]);
-  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+// Rank-1 update of column j (compile-time) on entries j+1..31 of one row held as packed
+// pairs: a[k] -= l * cj[k], cj the published column (16-byte aligned shared memory).
+__device__ __forceinline__ void row_update(uint64_t (&a)[16], int j, float l, const float* cj) {
+  const float nl = -l;
+  int p0 = (j + 1) >> 1;
+  if ((j + 1) & 1) {  // odd first entry: the high half alone, then whole pairs
+    const uint64_t v = a[p0];
+    a[p0] = pack2(lo_of(v), fmaf(nl, cj[j + 1], hi_of(v)));
+    ++p0;
+  }
+  const uint64_t nl2 = pack2(nl, nl);
+#pragma unroll
+  for (int q = p0 >> 1; q < 8; ++q) {
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(cj + 4 * q);
+    if (2 * q >= p0) a[2 * q] = ffma2_u64(nl2, v.x, a[2 * q]);
+    a[2 * q + 1] = ffma2_u64(nl2, v.y, a[2 * q + 1]);
+  }
+}
+
+// One warp of a panel (rows k0..n-1 of the w <= 32 panel columns, lane = row, entries as
+// packed pairs in registers), right-looking, with no synchronisation beyond the warp: every
+// warp holds the panel's diagonal block too (d: lane = diagonal row; the first warp's own
+// rows are that block, kDiag) and factors its copy in step with the others, so it has the
+// column it needs without waiting for another warp. Per column j: the pivot comes from lane
+// j by shuffle (prepared in the previous column from that lane's registers: look-ahead);
+// r = rsqrt(pivot); the diagonal row gets pivot * r = sqrt(pivot) and the rows below
+// a * r; the copy's column goes to this warp's ping-pong buffer (cw: 2 x 32 floats); after
+// __syncwarp every row takes the rank-1 update of its remaining entries from broadcast
+// reads. The diagonal block's factor and the solve of the rows below are one pass, and every
+// warp computes the same copy with the same operations, so the result does not depend on
+// the number of warps. Entries above the diagonal of the block are garbage, never read.
+template <bool kDiag>
+__device__ __forceinline__ void panel_rows_factor(uint64_t (&d)[16], uint64_t (&a)[16], int w,
+                                                  int lane, float* cw) {
+  float dnext = lo_of(d[0]);  // lane j's value is pivot j
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     if (j < w) {
-      const float d = db[j & 1];
-      const float r = mid_rsqrt(d);
-      const uint64_t cur = a[j >> 1];
-      const float l = ((j & 1) ? hi_of(cur) : lo_of(cur)) * r;
-      a[j >> 1] = (j & 1) ? pack2(lo_of(cur), l) : pack2(l, hi_of(cur));
-      float* cj = cb + (j & 1) * 32;
-      if (tid > j && tid < w) cj[tid] = l;
-      if (tid == j + 1 && j + 1 < w) {
-        const uint64_t nx = a[(j + 1) >> 1];
-        db[(j + 1) & 1] = fmaf(-l, l, ((j + 1) & 1) ? hi_of(nx) : lo_of(nx));
+      const float piv = __shfl_sync(0xffffffffu, dnext, j);
+      const float r = mid_rsqrt(piv);
+      const uint64_t cd = d[j >> 1];
+      const float ld = ((j & 1) ? hi_of(cd) : lo_of(cd)) * r;
+      d[j >> 1] = (j & 1) ? pack2(lo_of(cd), ld) : pack2(ld, hi_of(cd));
+      float la = 0.f;
+      if (!kDiag) {
+        const uint64_t ca = a[j >> 1];
+        la = ((j & 1) ? hi_of(ca) : lo_of(ca)) * r;
+        a[j >> 1] = (j & 1) ? pack2(lo_of(ca), la) : pack2(la, hi_of(ca));
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      if (tid > j && j + 1 < 32) {
-        // entries j+1..31 of this row (for a row of the diagonal block only those <= tid
-        // matter; the others lie above the diagonal and are never read)
-        const float nl = -l;
-        int p0 = (j + 1) >> 1;
-        if ((j + 1) & 1) {  // odd first entry: the high half alone, then whole pairs
-          const uint64_t v = a[p0];
-          a[p0] = pack2(lo_of(v), fmaf(nl, cj[j + 1], hi_of(v)));
-          ++p0;
-        }
-        const uint64_t nl2 = pack2(nl, nl);
-#pragma unroll
-        for (int q = p0 >> 1; q < 8; ++q) {
-          const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(cj + 4 * q);
-          if (2 * q >= p0) a[2 * q] = ffma2_u64(nl2, v.x, a[2 * q]);
-          a[2 * q + 1] = ffma2_u64(nl2, v.y, a[2 * q + 1]);
-        }
+      float* cj = cw + (j & 1) * 32;
+      if (lane > j && lane < w) cj[lane] = ld;
+      if (j + 1 < w) {
+        // the same operands as the update below applies to d[j+1] in lane j+1
+        const uint64_t nx = d[(j + 1) >> 1];
+        dnext = fmaf(-ld, ld, ((j + 1) & 1) ? hi_of(nx) : lo_of(nx));
+      }
+      __syncwarp();
+      if (j + 1 < 32) {
+        row_update(d, j, ld, cj);  // rows <= j change only entries above their diagonal
+        if (!kDiag) row_update(a, j, la, cj);
       }
     }
   }
 }
 
 // The panel in shared memory: rows 0..rows-1 at P + t * ld (P = its element (k0, k0)).
-__device__ __forceinline__ void smem_panel(float* P, int ld, int rows, int w, int tid, float* cb,
-                                           float* db) {
+// cb: 8 x 64 floats, 16-byte aligned (each warp's column buffer).
+__device__ __forceinline__ void smem_panel(float* P, int ld, int rows, int w, int tid, float* cb) {
   const int nthr = (rows + 31) & ~31;
   if (tid >= nthr) return;
+  const int lane = tid & 31, wp = tid >> 5;
   const bool own = tid < rows;
+  float* dp = P + lane * ld;  // this lane's row of the diagonal block
   float* rp = P + (own ? tid : 0) * ld;
-  uint64_t a[16];  // a[p] = entries (2p, 2p+1) of this thread's row, for the packed FMA
+  uint64_t d[16], a[16];
 #pragma unroll
   for (int p = 0; p < 16; ++p)
-    a[p] = pack2((own && 2 * p < w) ? rp[2 * p] : 0.f, (own && 2 * p + 1 < w) ? rp[2 * p + 1] : 0.f);
-  panel_rows_factor(a, w, tid, nthr, cb, db);
+    d[p] = pack2((lane < w && 2 * p < w) ? dp[2 * p] : 0.f,
+                 (lane < w && 2 * p + 1 < w) ? dp[2 * p + 1] : 0.f);
+  float* cw = cb + wp * 64;
+  if (wp > 0) {
+    // a warp below the diagonal block: w == 32 (only the last panel is narrower, and it
+    // has no rows below its diagonal block)
+#pragma unroll
+    for (int p = 0; p < 16; ++p)
+      a[p] = pack2(own ? rp[2 * p] : 0.f, own ? rp[2 * p + 1] : 0.f);
+  }
+  // every warp has read the diagonal block before the first warp writes it back
+  asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+  if (wp == 0) {
+    panel_rows_factor<true>(d, a, w, lane, cw);
+    if (lane < w) {
+#pragma unroll
+      for (int p = 0; p < 16; ++p) {
+        if (2 * p < w) dp[2 * p] = lo_of(d[p]);
+        if (2 * p + 1 < w) dp[2 * p + 1] = hi_of(d[p]);
+      }
+    }
+    return;
+  }
+  panel_rows_factor<false>(d, a, w, lane, cw);
   if (own) {
 #pragma unroll
     for (int p = 0; p < 16; ++p) {
-      if (2 * p < w) rp[2 * p] = lo_of(a[p]);
-      if (2 * p + 1 < w) rp[2 * p + 1] = hi_of(a[p]);
+      rp[2 * p] = lo_of(a[p]);
+      rp[2 * p + 1] = hi_of(a[p]);
     }
   }
 }
@@ -184,7 +222,7 @@ __device__ __forceinline__ void mid_update(float* As, int ld, int n, int k0, int
   }
 }
 
-// The panel's column buffer and pivots follow the matrix (offset in floats, 16-byte aligned).
+// The warps' column buffers follow the matrix (offset in floats, 16-byte aligned).
 __host__ __device__ __forceinline__ int mid_aux_offset(int n) { return (n * (n | 1) + 3) & ~3; }
 
 __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
@@ -193,8 +231,7 @@ __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
   griddep_launch();
   extern __shared__ float As[];
   const int ld = n | 1;
-  float* cb = As + mid_aux_offset(n);  // 2 x 32 floats, 16-byte aligned
-  float* db = cb + 64;
+  float* cb = As + mid_aux_offset(n);  // the warps' column buffers, 16-byte aligned
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int64_t m = blockIdx.x; m < batch; m += gridDim.x) {
     const float* Am = A + m * int64_t(n) * n;
@@ -205,7 +242,7 @@ __global__ void __launch_bounds__(kMidThreads, kMidCtasPerSm)
     __syncthreads();
     for (int k0 = 0; k0 < n; k0 += 32) {
       const int w = min(32, n - k0);
-      smem_panel(As + k0 * ld + k0, ld, n - k0, w, tid, cb, db);
+      smem_panel(As + k0 * ld + k0, ld, n - k0, w, tid, cb);
       __syncthreads();
       const int k1 = k0 + w;
       if (k1 < n) {
@@ -308,8 +345,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   extern __shared__ float sm[];
   float* P = sm;  // the current panel's rows, stride kXld
   float* cb = sm + kProws * kXld + 4 - (kProws * kXld) % 4;  // 16-byte aligned
-  float* db = cb + 64;
-  int* first = reinterpret_cast<int*>(db + 8);  // one per warp of the diagonal scan
+  int* first = reinterpret_cast<int*>(cb + 8 * 64);  // one per warp of the diagonal scan
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int64_t m = blockIdx.x; m < batch; m += gridDim.x) {
     const float* Am = A + m * int64_t(n) * n;
@@ -326,7 +362,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         if (c < w) P[r * kXld + c] = src[int64_t(k0 + r) * n + k0 + c];
       }
       __syncthreads();
-      smem_panel(P, kXld, rows, w, tid, cb, db);
+      smem_panel(P, kXld, rows, w, tid, cb);
       __syncthreads();
       for (int e = tid; e < rows * 32; e += kWideThreads) {  // the factored panel to L
         const int r = e >> 5, c = e & 31;
@@ -358,10 +394,10 @@ __global__ void __launch_bounds__(kWideThreads, 1)
 }
 
 size_t wide_smem_bytes() {
-  return (size_t(kProws * kXld + 4 - (kProws * kXld) % 4) + 64 + 8 + 8) * sizeof(float);
+  return (size_t(kProws * kXld + 4 - (kProws * kXld) % 4) + 8 * 64 + 8) * sizeof(float);
 }
 
-size_t mid_smem_bytes(int n) { return (size_t(mid_aux_offset(n)) + 72) * sizeof(float); }
+size_t mid_smem_bytes(int n) { return (size_t(mid_aux_offset(n)) + 4 * 64) * sizeof(float); }
 
 }  // namespace
 

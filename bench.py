@@ -26,6 +26,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import re
 import math
 import os
 import statistics
@@ -1004,7 +1005,13 @@ def run_ncu_target(args):
     from linalg_kernels_b200 import inputs
     from linalg_kernels_b200.cholesky import custom_kernel
 
-    cfg = inputs.GRID[args.config]
+    if args.config in inputs.GRID:
+        cfg = inputs.GRID[args.config]
+    else:  # any other shape, "b<batch>n<n>": spectral inputs, condition 1e3
+        m = re.fullmatch(r"b(\d+)n(\d+)", args.config)
+        if m is None:
+            raise SystemExit(f"--ncu-run: unknown config {args.config!r}")
+        cfg = inputs.Config(args.config, int(m.group(1)), int(m.group(2)), "spectral", 1e3, 7)
     dev = torch.device("cuda", 0)
     if not args.overlap:
         from linalg_kernels_b200 import _lib

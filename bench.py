@@ -816,6 +816,7 @@ def _bcast_ms(dist: Dist, dev, nbytes: int, reps: int = 10) -> float:
 
 def _multi_gpu(args, dist: Dist, dev, peaks) -> dict:
     from linalg_kernels_b200 import inputs
+    from linalg_kernels_b200.distributed import auto_queues
 
     out: dict = {}
     cp = _cyclic_parity(dist, dev)
@@ -835,7 +836,9 @@ def _multi_gpu(args, dist: Dist, dev, peaks) -> dict:
         "bcast_ms_all_panels_serial": _sig(sum(
             bc32 * (big.n - j * 256) / big.n for j in range(r["lay"].nblocks))),
         "parallelism": f"1-D block-column-cyclic over {dist.world} GPUs (256-wide blocks), "
-                       f"NCCL broadcast of each factored panel, strong scaling"}
+                       f"NCCL broadcast of each factored panel, depth-2 look-ahead on a chain "
+                       f"queue beside the trailing update on a bulk queue, GEMM CTA caps "
+                       f"{auto_queues(dist.world)}, strong scaling"}
     for name in ("b640n512", "b60n1024"):
         sh = _sharded(dist, inputs.GRID[name], dev, steps=10, warmup=3)
         gates.append(sh.pop("parity"))

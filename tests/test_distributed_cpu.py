@@ -89,7 +89,8 @@ def _worker(rank, world, port, n, bs, seed, out_dir, paired=True, split=None):
                                                      (4, 520, 32, True, None),
                                                      (3, 260, 32, True, True),
                                                      (2, 300, 64, False, True),
-                                                     (4, 520, 32, True, True)])
+                                                     (4, 520, 32, True, True),
+                                                     (8, 680, 32, True, None)])
 def test_block_cyclic_gloo_matches_cholesky(tmp_path, world, n, bs, paired, split):
     # paired: every other update of the blocks right of the look-ahead block is deferred
     # and applied for two panels at once; split (split_send, off by default): each block is
